@@ -1,0 +1,143 @@
+/*
+ * polarquant_b200 -- C ABI of the B200 (sm_100a) encode and ADC-search library.
+ *
+ * Drop-in boundary for the hot path of the `remex` package
+ * (oaustegard/polarquant).  The reference is pure Python/NumPy, so it has no
+ * FFI of its own; each entry point below replaces the NumPy expression named
+ * in its comment, and the Python package `polarquant_b200` binds these
+ * symbols through ctypes behind the reference's Quantizer / CompressedVectors
+ * / PackedVectors / IVFCoarseIndex API.
+ *
+ * Conventions
+ *  - Every pointer is device memory owned by the caller, except where noted.
+ *  - Packed corpora use the reference's MSB-first row layout
+ *    (remex/packing.py:18-75, row-padded as remex/core.py:203-223) with a
+ *    device row stride `ldb` (bytes, a multiple of 16, >= packed bytes of one
+ *    row); buffers holding packed rows carry >= 64 bytes of slack after the
+ *    last row.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are
+ *    asynchronous: they enqueue work and return.
+ *  - Return value: PQ_OK (0) or a negative PQ_ERR_* code; pq_last_error()
+ *    gives the message of the last failure on the calling thread.  No C++
+ *    exception crosses the ABI.
+ *  - Scratch memory is caller-provided (`ws`, `ws_bytes`); the matching
+ *    *_workspace_bytes() function gives the size needed.
+ *  - Top-k outputs are ordered by score descending, ties by id ascending;
+ *    unused slots hold id -1 and score -inf.
+ */
+#ifndef POLARQUANT_B200_H
+#define POLARQUANT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PQ_OK 0
+#define PQ_ERR_INVALID (-1)     /* bad argument (message says which) */
+#define PQ_ERR_CUDA (-2)        /* CUDA runtime / launch failure */
+#define PQ_ERR_WORKSPACE (-3)   /* workspace too small */
+#define PQ_ERR_UNSUPPORTED (-4) /* shape outside what the kernels handle */
+#define PQ_ERR_DEVICE (-5)      /* a kernel reported a device-side failure */
+
+/* Largest k (or candidate count) of the fused top-k kernels. */
+#define PQ_TOPK_MAX 2048
+
+/* Library version (major*10000 + minor*100 + patch). */
+int pq_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* pq_last_error(void);
+
+/* Synchronises the current device and reports (then clears) the first
+ * device-side failure recorded by a kernel whose bounded wait ran out:
+ * *code = 0 when none.  Returns PQ_ERR_CUDA if the synchronisation fails. */
+int pq_device_status(int* code);
+
+/* Packed bytes of one row of d codes at `bits` (remex/packing.py:130-150). */
+int64_t pq_row_bytes(int d, int bits);
+
+/* ---------------------------------------------------------------------------
+ * Query rotation: Y = X @ R^T (nq x d, f32), i.e. q_rot = R @ q per query.
+ * Replaces `self.R @ query` (remex/core.py:570, :615, :682; remex/ivf.py:249,
+ * :331) and `queries @ self.R.T` (remex/core.py:759).  Exact f32 products
+ * accumulated in f64, rounded once to f32.
+ * ------------------------------------------------------------------------- */
+int pq_rotate(const float* X, int64_t nq, int d, const float* R, float* Y, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * ADC scan + top-k.  Replaces, per query,
+ *   table = np.outer(R @ q, centroids)                     (remex/core.py:615-618)
+ *   scores = table[arange(d), codes >> shift].sum(1)*norms  (remex/core.py:792-859)
+ *   argpartition/argsort top-k                              (remex/core.py:631-636)
+ * for `search_adc` and (same scores, remex/core.py:534-580) `search`.
+ *
+ * packed/norms: n rows (stride ldb); qrot: nq x d rotated queries (f32);
+ * cent: 2^precision centroids of the Matryoshka level (remex/core.py:882-901);
+ * shift = bits - precision.  1 <= k <= n; k > PQ_TOPK_MAX (e.g. k >= n, the
+ * reference's full-argsort case) takes a sort-based path one query at a time.
+ * Output: nq x k, ids are row + row_offset.
+ * ------------------------------------------------------------------------- */
+size_t pq_adc_scan_workspace_bytes(int64_t n, int nq, int k);
+int pq_adc_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
+                int bits, int precision, const float* qrot, int nq, const float* cent, int k,
+                int64_t row_offset, float* out_scores, int64_t* out_ids, void* ws,
+                size_t ws_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Two-stage Matryoshka search.  Replaces Quantizer.search_twostage
+ * (remex/core.py:638-719): coarse ADC at `coarse_precision` over all rows,
+ * top-`candidates` (unordered, any tie order), then full-precision rescoring
+ * sum_j q_rot[j]*cent_full[code_j]*norm of those rows, top-k.
+ * candidates <= PQ_TOPK_MAX, candidates <= n, k <= candidates.
+ * cent_coarse: 2^coarse_precision centroids; cent_full: 2^bits centroids.
+ * ------------------------------------------------------------------------- */
+size_t pq_twostage_workspace_bytes(int64_t n, int nq, int candidates);
+int pq_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
+                int bits, int coarse_precision, const float* qrot, int nq,
+                const float* cent_coarse, const float* cent_full, int candidates, int k,
+                int64_t row_offset, float* out_scores, int64_t* out_ids, void* ws,
+                size_t ws_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Full-precision rescoring of given rows + top-k (stage 2 of
+ * remex/core.py:706-719 and remex/ivf.py:422-436).  cand: nq x C local row
+ * ids (entries < 0 are skipped).  Output ids are row + row_offset.
+ * ------------------------------------------------------------------------- */
+int pq_rerank(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
+              int bits, const float* qrot, int nq, const float* cent_full, const int64_t* cand,
+              int C, int k, int64_t row_offset, float* out_scores, int64_t* out_ids,
+              void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Merge of per-part top-k lists: in_s/in_ids are parts x nq x kin (as written
+ * by the per-rank scans, ids already global); out is nq x k, k <= kin*parts,
+ * k <= PQ_TOPK_MAX.  Used after the NCCL all-gather of the row-sharded search.
+ * ------------------------------------------------------------------------- */
+int pq_topk_merge(const float* in_s, const int64_t* in_ids, int parts, int nq, int kin, int k,
+                  float* out_s, int64_t* out_ids, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Packed-row utilities (remex/core.py:161-201, :254-293).
+ * pq_unpack_rows: codes (n x d uint8, row stride d) = row codes >> shift.
+ * pq_unpack_at: same for rows idx[0..m) (gather).
+ * pq_repack: Matryoshka at_precision(target_bits): rows re-packed at
+ *   target_bits from codes >> (bits - target_bits); out stride ldb_out.
+ * pq_pack_codes: pack an (n x d) uint8 code matrix into rows of stride ldb.
+ * ------------------------------------------------------------------------- */
+int pq_unpack_rows(const uint8_t* packed, int64_t ldb, int64_t n, int d, int bits, int shift,
+                   uint8_t* out, void* stream);
+int pq_unpack_at(const uint8_t* packed, int64_t ldb, const int64_t* idx, int64_t m, int d,
+                 int bits, int shift, uint8_t* out, void* stream);
+int pq_repack(const uint8_t* packed, int64_t ldb, int64_t n, int d, int bits, int target_bits,
+              uint8_t* out, int64_t ldb_out, void* stream);
+int pq_pack_codes(const uint8_t* codes, int64_t n, int d, int bits, uint8_t* out, int64_t ldb,
+                  void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* POLARQUANT_B200_H */

@@ -1,0 +1,589 @@
+"""B200 drop-in for remex.core: Quantizer, CompressedVectors, PackedVectors.
+
+Same constructors, method names, argument meanings, return types and errors
+as remex/core.py.  The corpus lives on the GPU as packed rows (the reference's
+row-padded byte layout with a 16-byte-aligned device stride) plus f32 norms;
+encode, rotation, ADC scans, top-k and rerank run as kernels of the
+polarquant_b200 CUDA library (include/polarquant_b200.h).  Host arrays
+(``indices``, ``norms``, ``_packed``) are produced on demand.
+
+Differences from the reference, by design:
+  * ``search()`` is served by the ADC scan; the scores equal the cached f32
+    path's (remex/core.py:534-580 vs :582-636, equal to rtol 1e-5 by the
+    reference's own tests), so no n x d f32 ``_x_hat_rot`` cache is built and
+    ``_x_hat_rot`` stays ``None``.
+  * ``resident_bytes`` counts device bytes plus any host copies made.
+  * Extra batch entry points (``search_adc_many``, ``search_twostage_many``)
+    run many queries per launch.
+"""
+
+from __future__ import annotations
+
+from typing import Iterable, Optional, Tuple
+
+import numpy as np
+import torch
+
+from . import _lib
+from .device import (alloc_rows, check_device_errors, ptr, require_cuda, row_stride,
+                     rows_to_device, rows_to_host, stream_ptr, to_device_f32, topk_to_numpy,
+                     workspace)
+from .packing import pack, packed_nbytes, pack_rows, unpack, unpack_rows
+from .params import haar_rotation, lloyd_max_codebook, nested_codebooks
+
+TOPK_MAX = _lib.PQ_TOPK_MAX
+
+
+# ---------------------------------------------------------------------------
+# Device corpus storage shared by both containers
+# ---------------------------------------------------------------------------
+
+class _DeviceRows:
+    """Packed rows (stride ldb) + f32 norms on one CUDA device."""
+
+    __slots__ = ("buf", "norms", "n", "d", "bits", "ldb", "device")
+
+    def __init__(self, buf, norms, n, d, bits, ldb, device):
+        self.buf, self.norms, self.n, self.d = buf, norms, int(n), int(d)
+        self.bits, self.ldb, self.device = int(bits), int(ldb), device
+
+    @classmethod
+    def from_codes(cls, indices: np.ndarray, norms: np.ndarray, d: int, bits: int):
+        dev = require_cuda()
+        idx = np.ascontiguousarray(indices, dtype=np.uint8).reshape(-1, d)
+        n = idx.shape[0]
+        ldb = row_stride(d, bits)
+        buf = alloc_rows(n, ldb, dev)
+        nrm = to_device_f32(np.asarray(norms, np.float32).reshape(n), dev)
+        if n:
+            codes = torch.from_numpy(idx).to(dev)
+            _lib.call("pq_pack_codes", ptr(codes), n, d, bits, ptr(buf), ldb, stream_ptr(dev))
+        return cls(buf, nrm, n, d, bits, ldb, dev)
+
+    @classmethod
+    def from_rows(cls, rows: np.ndarray, norms: np.ndarray, d: int, bits: int):
+        dev = require_cuda()
+        ldb = row_stride(d, bits)
+        rows = np.asarray(rows, dtype=np.uint8)
+        n = rows.shape[0]
+        buf = rows_to_device(rows, ldb, dev)
+        nrm = to_device_f32(np.asarray(norms, np.float32).reshape(n), dev)
+        return cls(buf, nrm, n, d, bits, ldb, dev)
+
+    @property
+    def row_bytes(self) -> int:
+        return packed_nbytes(1, self.d, self.bits)
+
+    def codes(self, shift: int = 0) -> torch.Tensor:
+        out = torch.empty((self.n, self.d), dtype=torch.uint8, device=self.device)
+        if self.n:
+            _lib.call("pq_unpack_rows", ptr(self.buf), self.ldb, self.n, self.d, self.bits, shift,
+                      ptr(out), stream_ptr(self.device))
+        return out
+
+    def codes_at(self, idx: np.ndarray, shift: int = 0) -> torch.Tensor:
+        ii = torch.from_numpy(np.ascontiguousarray(idx, dtype=np.int64)).to(self.device)
+        m = ii.numel()
+        if m and (int(ii.min()) < 0 or int(ii.max()) >= self.n):
+            raise IndexError("row index out of range")
+        out = torch.empty((m, self.d), dtype=torch.uint8, device=self.device)
+        if m:
+            _lib.call("pq_unpack_at", ptr(self.buf), self.ldb, ptr(ii), m, self.d, self.bits,
+                      shift, ptr(out), stream_ptr(self.device))
+        return out
+
+    def rows_host(self) -> np.ndarray:
+        return rows_to_host(self.buf, self.n, self.ldb, self.row_bytes)
+
+    def subset(self, idx) -> "_DeviceRows":
+        ii = np.asarray(idx, dtype=np.int64).reshape(-1)
+        if ii.size and (ii.min() < -self.n or ii.max() >= self.n):
+            raise IndexError("row index out of range")
+        ii = np.where(ii < 0, ii + self.n, ii)
+        t = torch.from_numpy(ii).to(self.device)
+        m = len(ii)
+        buf = alloc_rows(m, self.ldb, self.device)
+        if m:
+            buf[: m * self.ldb].view(m, self.ldb).copy_(
+                self.buf[: self.n * self.ldb].view(self.n, self.ldb).index_select(0, t))
+        return _DeviceRows(buf, self.norms.index_select(0, t).contiguous(), m, self.d,
+                           self.bits, self.ldb, self.device)
+
+    def at_precision(self, target_bits: int) -> "_DeviceRows":
+        ldb = row_stride(self.d, target_bits)
+        buf = alloc_rows(self.n, ldb, self.device)
+        if self.n:
+            _lib.call("pq_repack", ptr(self.buf), self.ldb, self.n, self.d, self.bits,
+                      target_bits, ptr(buf), ldb, stream_ptr(self.device))
+        return _DeviceRows(buf, self.norms.clone(), self.n, self.d, target_bits, ldb,
+                           self.device)
+
+    @property
+    def device_bytes(self) -> int:
+        return self.buf.numel() + self.norms.numel() * 4
+
+
+def _validate_bits(bits: int) -> None:
+    if bits < 1 or bits > 8:
+        raise ValueError(f"bits must be 1-4 or 8, got {bits}")
+    if bits in (5, 6, 7):
+        raise ValueError(
+            f"bits={bits} is not supported. Use 1-4 or 8 bits. "
+            f"5-7 bit widths offer negligible benefit over 4-bit or 8-bit.")
+
+
+class CompressedVectors:
+    """Encoded corpus (remex/core.py:10-117), resident on the GPU.
+
+    ``indices`` (n, d) uint8 and ``norms`` (n,) f32 are host views produced
+    on first access; the device holds packed rows and norms.
+    """
+
+    def __init__(self, indices: np.ndarray, norms: np.ndarray, d: int, bits: int):
+        idx = np.asarray(indices, dtype=np.uint8)
+        self._rows = None
+        self._h_indices = idx.reshape(-1, int(d))
+        self._h_norms = np.asarray(norms, dtype=np.float32).reshape(-1)
+        self.d = int(d)
+        self.bits = int(bits)
+        self.n = self._h_indices.shape[0]
+        self._x_hat_rot = None
+
+    @classmethod
+    def _from_device(cls, rows: _DeviceRows) -> "CompressedVectors":
+        obj = cls.__new__(cls)
+        obj._rows = rows
+        obj._h_indices = None
+        obj._h_norms = None
+        obj.d, obj.bits, obj.n = rows.d, rows.bits, rows.n
+        obj._x_hat_rot = None
+        return obj
+
+    # -- device side ------------------------------------------------------
+    def _device(self) -> _DeviceRows:
+        if self._rows is None:
+            self._rows = _DeviceRows.from_codes(self._h_indices, self._h_norms, self.d, self.bits)
+        return self._rows
+
+    # -- host views -------------------------------------------------------
+    @property
+    def indices(self) -> np.ndarray:
+        if self._h_indices is None:
+            self._h_indices = self._rows.codes().cpu().numpy()
+        return self._h_indices
+
+    @indices.setter
+    def indices(self, value) -> None:
+        self._h_indices = np.asarray(value, dtype=np.uint8)
+        self.n = self._h_indices.shape[0]
+        self._rows = None
+
+    @property
+    def norms(self) -> np.ndarray:
+        if self._h_norms is None:
+            self._h_norms = self._rows.norms.cpu().numpy()
+        return self._h_norms
+
+    @norms.setter
+    def norms(self, value) -> None:
+        self._h_norms = np.asarray(value, dtype=np.float32)
+        self._rows = None
+
+    def subset(self, idx: np.ndarray) -> "CompressedVectors":
+        return CompressedVectors._from_device(self._device().subset(idx))
+
+    @property
+    def nbytes(self) -> int:
+        return packed_nbytes(self.n, self.d, self.bits) + self.n * 4
+
+    @property
+    def nbytes_unpacked(self) -> int:
+        return self.n * self.d + self.n * 4
+
+    @property
+    def compression_ratio(self) -> float:
+        return (self.n * self.d * 4) / self.nbytes
+
+    @property
+    def resident_bytes(self) -> int:
+        total = 0 if self._rows is None else self._rows.device_bytes
+        if self._h_indices is not None:
+            total += self._h_indices.nbytes
+        if self._h_norms is not None:
+            total += self._h_norms.nbytes
+        return total
+
+    def drop_cache(self) -> None:
+        self._x_hat_rot = None
+
+    def save(self, path: str) -> None:
+        """Same .npz keys and bytes as remex/core.py:64-74."""
+        if self._rows is not None and (self.d * self.bits) % 8 == 0:
+            flat = self._rows.rows_host().ravel()
+        else:
+            flat = pack(self.indices.ravel(), self.bits)
+        np.savez_compressed(path, packed_indices=flat, norms=self.norms,
+                            d=np.int32(self.d), bits=np.int32(self.bits), n=np.int32(self.n))
+
+    @classmethod
+    def load(cls, path: str) -> "CompressedVectors":
+        """remex/core.py:76-91 (also reads the legacy unpacked 'indices' key)."""
+        data = np.load(path)
+        d, bits, n = int(data["d"]), int(data["bits"]), int(data["n"])
+        norms = data["norms"]
+        if "packed_indices" in data:
+            flat = data["packed_indices"]
+            if (d * bits) % 8 == 0:
+                rows = flat[: n * packed_nbytes(1, d, bits)].reshape(n, -1) if n else \
+                    np.zeros((0, packed_nbytes(1, d, bits)), np.uint8)
+                return cls._from_device(_DeviceRows.from_rows(rows, norms, d, bits))
+            return cls(unpack(flat, bits, n * d).reshape(n, d), norms, d, bits)
+        return cls(data["indices"], norms, d, bits)
+
+    def save_arrow(self, path: str, seed: Optional[int] = None, **extra_metadata):
+        PackedVectors.from_compressed(self).save_arrow(path, seed=seed, **extra_metadata)
+
+    @classmethod
+    def load_arrow(cls, path: str) -> "CompressedVectors":
+        return PackedVectors.load_arrow(path).to_compressed()
+
+
+class PackedVectors:
+    """Packed storage (remex/core.py:120-439), resident on the GPU."""
+
+    def __init__(self, packed: np.ndarray, norms: np.ndarray, n: int, d: int, bits: int):
+        self._rows = _DeviceRows.from_rows(np.asarray(packed, np.uint8).reshape(int(n), -1),
+                                           norms, d, bits)
+        self._init_meta()
+
+    def _init_meta(self) -> None:
+        r = self._rows
+        self.n, self.d, self.bits = r.n, r.d, r.bits
+        self._row_bytes = packed_nbytes(1, self.d, self.bits)
+        self._row_aligned = (self.d * self.bits) % 8 == 0
+        self._h_packed = None
+        self._h_norms = None
+
+    @classmethod
+    def _wrap(cls, rows: _DeviceRows) -> "PackedVectors":
+        obj = cls.__new__(cls)
+        obj._rows = rows
+        obj._init_meta()
+        return obj
+
+    def _device(self) -> _DeviceRows:
+        return self._rows
+
+    @property
+    def _packed(self) -> np.ndarray:
+        if self._h_packed is None:
+            self._h_packed = self._rows.rows_host()
+        return self._h_packed
+
+    @property
+    def norms(self) -> np.ndarray:
+        if self._h_norms is None:
+            self._h_norms = self._rows.norms.cpu().numpy()
+        return self._h_norms
+
+    def unpack_rows(self, start: int, end: int) -> np.ndarray:
+        start, end = max(0, int(start)), min(self.n, int(end))
+        if end <= start:
+            return np.zeros((0, self.d), np.uint8)
+        return self._rows.codes_at(np.arange(start, end)).cpu().numpy()
+
+    def unpack_at(self, idx: np.ndarray) -> np.ndarray:
+        idx = np.asarray(idx)
+        if idx.ndim == 0:
+            idx = idx.reshape(1)
+        return self._rows.codes_at(idx).cpu().numpy()
+
+    @classmethod
+    def from_compressed(cls, compressed: CompressedVectors) -> "PackedVectors":
+        r = compressed._device()
+        return cls._wrap(_DeviceRows(r.buf.clone(), r.norms.clone(), r.n, r.d, r.bits, r.ldb,
+                                     r.device))
+
+    @classmethod
+    def from_rows(cls, rows: Iterable, norms: np.ndarray, d: int, bits: int) -> "PackedVectors":
+        lst = [np.frombuffer(r, dtype=np.uint8) if isinstance(r, (bytes, bytearray))
+               else np.asarray(r, dtype=np.uint8) for r in rows]
+        packed = np.stack(lst) if lst else np.zeros((0, packed_nbytes(1, d, bits)), np.uint8)
+        return cls(packed, np.asarray(norms, dtype=np.float32), len(lst), d, bits)
+
+    def at_precision(self, target_bits: int) -> "PackedVectors":
+        if target_bits < 1 or target_bits > self.bits:
+            raise ValueError(f"target_bits must be 1-{self.bits}, got {target_bits}")
+        if target_bits == self.bits:
+            return self
+        return PackedVectors._wrap(self._rows.at_precision(target_bits))
+
+    def to_compressed(self) -> CompressedVectors:
+        r = self._rows
+        return CompressedVectors._from_device(
+            _DeviceRows(r.buf.clone(), r.norms.clone(), r.n, r.d, r.bits, r.ldb, r.device))
+
+    def subset(self, idx: np.ndarray) -> "PackedVectors":
+        return PackedVectors._wrap(self._rows.subset(idx))
+
+    @property
+    def nbytes(self) -> int:
+        return self.n * self._row_bytes + self.n * 4
+
+    @property
+    def resident_bytes(self) -> int:
+        total = self._rows.device_bytes
+        if self._h_packed is not None:
+            total += self._h_packed.nbytes
+        if self._h_norms is not None:
+            total += self._h_norms.nbytes
+        return total
+
+    @property
+    def compression_ratio(self) -> float:
+        return (self.n * self.d * 4) / self.nbytes
+
+    def save(self, path: str) -> None:
+        """remex/core.py:326-335."""
+        np.savez_compressed(path, packed_indices=self._packed.ravel(), norms=self.norms,
+                            d=np.int32(self.d), bits=np.int32(self.bits), n=np.int32(self.n))
+
+    @classmethod
+    def load(cls, path: str) -> "PackedVectors":
+        data = np.load(path)
+        d, bits, n = int(data["d"]), int(data["bits"]), int(data["n"])
+        rb = packed_nbytes(1, d, bits)
+        return cls(data["packed_indices"].reshape(n, rb), data["norms"], n, d, bits)
+
+    def save_arrow(self, path: str, seed: Optional[int] = None, **extra_metadata):
+        """Arrow IPC layout of remex/core.py:349-401."""
+        try:
+            import pyarrow as pa
+            import pyarrow.feather as feather
+        except ImportError:
+            raise ImportError("pyarrow is required for Arrow IPC format: pip install pyarrow")
+        meta = {b"d": str(self.d).encode(), b"bits": str(self.bits).encode(),
+                b"n": str(self.n).encode()}
+        if seed is not None:
+            meta[b"seed"] = str(seed).encode()
+        for k, v in extra_metadata.items():
+            meta[k.encode() if isinstance(k, str) else k] = str(v).encode()
+        schema = pa.schema([pa.field("norms", pa.float32()),
+                            pa.field("packed_indices", pa.binary(self._row_bytes))],
+                           metadata=meta)
+        arr = pa.FixedSizeBinaryArray.from_buffers(
+            pa.binary(self._row_bytes), self.n, [None, pa.py_buffer(self._packed.tobytes())])
+        table = pa.table({"norms": pa.array(self.norms, type=pa.float32()),
+                          "packed_indices": arr}, schema=schema)
+        feather.write_feather(table, path)
+
+    @classmethod
+    def load_arrow(cls, path: str, memory_map: bool = False) -> "PackedVectors":
+        try:
+            import pyarrow.feather as feather
+        except ImportError:
+            raise ImportError("pyarrow is required for Arrow IPC format: pip install pyarrow")
+        table = feather.read_table(path, memory_map=memory_map)
+        meta = table.schema.metadata
+        d, bits, n = int(meta[b"d"]), int(meta[b"bits"]), int(meta[b"n"])
+        rb = packed_nbytes(1, d, bits)
+        norms = table.column("norms").to_numpy().astype(np.float32)
+        col = table.column("packed_indices").combine_chunks()
+        flat = np.frombuffer(col.buffers()[1], dtype=np.uint8)[col.offset * rb:
+                                                               (col.offset + n) * rb]
+        return cls(flat.reshape(n, rb).copy(), norms, n, d, bits)
+
+
+# ---------------------------------------------------------------------------
+# Quantizer
+# ---------------------------------------------------------------------------
+
+class _DeviceParams:
+    """Per-device copies of the Quantizer's tables."""
+
+    def __init__(self, q: "Quantizer", dev: torch.device):
+        self.device = dev
+        self.R = torch.from_numpy(np.ascontiguousarray(q.R)).to(dev)
+        self.RT = None
+        self.boundaries = torch.from_numpy(np.ascontiguousarray(q.boundaries)).to(dev)
+        self.cent = {p: torch.from_numpy(np.ascontiguousarray(t)).to(dev)
+                     for p, t in q._nested.items()}
+        self.cent[q.bits] = torch.from_numpy(np.ascontiguousarray(q.centroids)).to(dev)
+
+
+class Quantizer:
+    """Drop-in for remex.Quantizer (remex/core.py:442-901) on a B200."""
+
+    def __init__(self, d: int, bits: int = 4, seed: int = 42):
+        _validate_bits(bits)
+        self.d = d
+        self.bits = bits
+        self.seed = seed
+        self.R = haar_rotation(d, seed)
+        self.boundaries, self.centroids = lloyd_max_codebook(d, bits)
+        self._nested = nested_codebooks(d, bits)
+        self._dev = {}
+
+    # -- device state -------------------------------------------------------
+    def _params(self, dev: Optional[torch.device] = None) -> _DeviceParams:
+        dev = dev or require_cuda()
+        key = dev.index
+        if key not in self._dev:
+            self._dev[key] = _DeviceParams(self, dev)
+        return self._dev[key]
+
+    def _resolve_centroids(self, compressed, precision: Optional[int]) -> np.ndarray:
+        """remex/core.py:882-892."""
+        if precision is None:
+            return self.centroids
+        if precision < 1 or precision > self.bits:
+            raise ValueError(f"precision must be 1-{self.bits}, got {precision}")
+        return self._nested[precision]
+
+    def _level(self, precision: Optional[int]) -> int:
+        self._resolve_centroids(None, precision)
+        return self.bits if precision is None else int(precision)
+
+    def _rotate(self, X, dev: torch.device) -> torch.Tensor:
+        Xd = to_device_f32(X, dev)
+        if Xd.dim() == 1:
+            Xd = Xd.unsqueeze(0)
+        if Xd.shape[1] != self.d:
+            raise ValueError(f"Expected d={self.d}, got {Xd.shape[1]}")
+        Y = torch.empty_like(Xd)
+        _lib.call("pq_rotate", ptr(Xd), Xd.shape[0], self.d, ptr(self._params(dev).R), ptr(Y),
+                  stream_ptr(dev))
+        return Y
+
+    @staticmethod
+    def _rows_of(compressed) -> _DeviceRows:
+        if isinstance(compressed, (CompressedVectors, PackedVectors)):
+            return compressed._device()
+        raise TypeError(f"expected CompressedVectors or PackedVectors, got "
+                        f"{type(compressed).__name__}")
+
+    def _check_corpus(self, rows: _DeviceRows) -> None:
+        if rows.d != self.d or rows.bits != self.bits:
+            raise ValueError(f"corpus (d={rows.d}, bits={rows.bits}) does not match quantizer "
+                             f"(d={self.d}, bits={self.bits})")
+
+    # -- encode ---------------------------------------------------------------
+    def encode(self, X) -> CompressedVectors:
+        """Quantize (n, d) vectors (remex/core.py:484-511) on the GPU."""
+        from .encode import encode_rows
+        return CompressedVectors._from_device(encode_rows(self, X))
+
+    def decode(self, compressed, precision: Optional[int] = None) -> np.ndarray:
+        """remex/core.py:513-532."""
+        from .encode import decode_rows
+        p = self._level(precision)
+        return decode_rows(self, self._rows_of(compressed), p).cpu().numpy()
+
+    def mse(self, X, precision: Optional[int] = None) -> float:
+        """remex/core.py:780-786."""
+        comp = self.encode(X)
+        X_hat = self.decode(comp, precision=precision)
+        Xh = np.asarray(X, np.float32)
+        if Xh.ndim == 1:
+            Xh = Xh[None]
+        return float(np.mean(np.sum((Xh - X_hat) ** 2, axis=1)))
+
+    # -- search -------------------------------------------------------------
+    def _scan(self, rows: _DeviceRows, qrot: torch.Tensor, k: int, p: int):
+        """Top-min(k, n) ADC results for each row of qrot, on the device."""
+        dev = rows.device
+        nq = qrot.shape[0]
+        K = min(int(k), rows.n)
+        if K <= 0 or nq == 0:
+            return (torch.empty((nq, 0), dtype=torch.float32, device=dev),
+                    torch.empty((nq, 0), dtype=torch.int64, device=dev))
+        cent = self._params(dev).cent[p]
+        ws = workspace(_lib.query("pq_adc_scan_workspace_bytes", rows.n, nq, K), dev)
+        out_s = torch.empty((nq, K), dtype=torch.float32, device=dev)
+        out_i = torch.empty((nq, K), dtype=torch.int64, device=dev)
+        _lib.call("pq_adc_scan", ptr(rows.buf), rows.ldb, ptr(rows.norms), rows.n, rows.d,
+                  rows.bits, p, ptr(qrot), nq, ptr(cent), K, 0, ptr(out_s), ptr(out_i),
+                  ptr(ws), ws.numel(), stream_ptr(dev))
+        return out_s, out_i
+
+    def _twostage(self, rows: _DeviceRows, qrot: torch.Tensor, k: int, candidates: int,
+                  cp: int):
+        dev = rows.device
+        nq = qrot.shape[0]
+        ck = min(int(candidates), rows.n)
+        if ck <= 0 or nq == 0 or k <= 0:
+            return (torch.empty((nq, 0), dtype=torch.float32, device=dev),
+                    torch.empty((nq, 0), dtype=torch.int64, device=dev))
+        if ck >= rows.n:
+            # Every row is a candidate: stage 2 alone decides (remex/core.py:701-702).
+            return self._scan(rows, qrot, min(k, rows.n), self.bits)
+        if ck > TOPK_MAX:
+            raise NotImplementedError(f"candidates={ck} exceeds the fused limit {TOPK_MAX}")
+        K = min(int(k), ck)
+        pr = self._params(dev)
+        ws = workspace(_lib.query("pq_twostage_workspace_bytes", rows.n, nq, ck), dev)
+        out_s = torch.empty((nq, K), dtype=torch.float32, device=dev)
+        out_i = torch.empty((nq, K), dtype=torch.int64, device=dev)
+        _lib.call("pq_twostage", ptr(rows.buf), rows.ldb, ptr(rows.norms), rows.n, rows.d,
+                  rows.bits, cp, ptr(qrot), nq, ptr(pr.cent[cp]), ptr(pr.cent[self.bits]), ck,
+                  K, 0, ptr(out_s), ptr(out_i), ptr(ws), ws.numel(), stream_ptr(dev))
+        return out_s, out_i
+
+    def search(self, compressed, query, k: int = 10, precision: Optional[int] = None):
+        """remex/core.py:534-580 (scores via the ADC scan)."""
+        if isinstance(compressed, PackedVectors):
+            raise TypeError(
+                "PackedVectors does not support cached search(). "
+                "Use search_adc() or search_twostage(), or convert "
+                "with packed.to_compressed() first.")
+        return self.search_adc(compressed, query, k=k, precision=precision)
+
+    def search_adc(self, compressed, query, k: int = 10, precision: Optional[int] = None,
+                   chunk_size: int = 4096):
+        """remex/core.py:582-636.  chunk_size is accepted; results do not depend on it."""
+        rows = self._rows_of(compressed)
+        self._check_corpus(rows)
+        p = self._level(precision)
+        qrot = self._rotate(query, rows.device)
+        s, i = self._scan(rows, qrot, k, p)
+        ids, sc = topk_to_numpy(s, i)
+        return ids[0], sc[0]
+
+    def search_adc_many(self, compressed, queries, k: int = 10,
+                        precision: Optional[int] = None):
+        """search_adc for each row of `queries`; returns (nq, min(k, n)) arrays."""
+        rows = self._rows_of(compressed)
+        self._check_corpus(rows)
+        p = self._level(precision)
+        s, i = self._scan(rows, self._rotate(queries, rows.device), k, p)
+        return topk_to_numpy(s, i)
+
+    def search_twostage(self, compressed, query, k: int = 10, candidates: int = 500,
+                        coarse_precision: Optional[int] = None, coarse_chunk_size: int = 4096):
+        """remex/core.py:638-719."""
+        ids, sc = self.search_twostage_many(compressed, query, k=k, candidates=candidates,
+                                            coarse_precision=coarse_precision)
+        return ids[0], sc[0]
+
+    def search_twostage_many(self, compressed, queries, k: int = 10, candidates: int = 500,
+                             coarse_precision: Optional[int] = None):
+        if coarse_precision is None:
+            coarse_precision = max(1, self.bits - 2)
+        cp = self._level(coarse_precision)
+        rows = self._rows_of(compressed)
+        self._check_corpus(rows)
+        s, i = self._twostage(rows, self._rotate(queries, rows.device), k, candidates, cp)
+        return topk_to_numpy(s, i)
+
+    def search_batch(self, compressed, queries, k: int = 10, precision: Optional[int] = None):
+        """remex/core.py:721-778: (n_queries, min(k, n)) indices and scores."""
+        if isinstance(compressed, PackedVectors):
+            raise TypeError(
+                "PackedVectors does not support cached search_batch(). "
+                "Use search_adc() or search_twostage(), or convert "
+                "with packed.to_compressed() first.")
+        Q = np.asarray(queries, dtype=np.float32) if not isinstance(queries, torch.Tensor) \
+            else queries
+        if Q.ndim == 1:
+            Q = Q[None]
+        return self.search_adc_many(compressed, Q, k=k, precision=precision)

@@ -1,0 +1,6 @@
+// Single translation unit for the library (device globals are shared across
+// the kernels without relocatable device code).
+#include "capi.cu"
+#include "scan.cu"
+#include "rotate.cu"
+#include "sort.cu"

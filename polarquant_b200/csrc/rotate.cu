@@ -1,0 +1,81 @@
+// Query rotation q_rot = R @ q for query batches (remex/core.py:615, :682,
+// :759; remex/ivf.py:331): Y = X @ R^T with X (nq x d) and R (d x d), f32 in
+// and out.  Products of the f32 inputs are exact in f64 and are accumulated
+// in f64, so Y is the correctly rounded f32 of the exact product (the
+// reference's sgemv result differs from it only by sgemv's own rounding).
+//
+// Work per call is nq * d^2 multiply-adds -- at most ~2.4e10 for a 10,000
+// query batch at d = 1536 -- which is small next to the scans it feeds, so a
+// register-tiled SIMT kernel is used rather than the tensor-core encode GEMM.
+#include "common.cuh"
+
+namespace pqb {
+
+constexpr int kRotTile = 64;   // queries x outputs per block
+constexpr int kRotK = 16;      // K slice staged in shared memory
+constexpr int kRotThreads = 256;  // 16 x 16 threads, 4 x 4 outputs each
+
+__global__ void __launch_bounds__(kRotThreads)
+rotate_kernel(const float* __restrict__ X, int64_t nq, int d, const float* __restrict__ R,
+              float* __restrict__ Y) {
+  __shared__ float xs[kRotK][kRotTile + 1];
+  __shared__ float rs[kRotK][kRotTile + 1];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t q0 = (int64_t)blockIdx.y * kRotTile;
+  const int o0 = blockIdx.x * kRotTile;
+  double acc[4][4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) acc[a][b] = 0.0;
+  for (int k0 = 0; k0 < d; k0 += kRotK) {
+    for (int i = threadIdx.x; i < kRotK * kRotTile; i += kRotThreads) {
+      const int row = i / kRotK, kk = i % kRotK;
+      const int64_t qi = q0 + row;
+      const int oi = o0 + row, k = k0 + kk;
+      xs[kk][row] = (qi < nq && k < d) ? X[qi * d + k] : 0.f;
+      rs[kk][row] = (oi < d && k < d) ? R[(int64_t)oi * d + k] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < kRotK; ++kk) {
+      double xv[4], rv[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) xv[a] = (double)xs[kk][ty + 16 * a];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) rv[b] = (double)rs[kk][tx + 16 * b];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][b] = fma(xv[a], rv[b], acc[a][b]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int64_t qi = q0 + ty + 16 * a;
+    if (qi >= nq) continue;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int oi = o0 + tx + 16 * b;
+      if (oi < d) Y[qi * d + oi] = (float)acc[a][b];
+    }
+  }
+}
+
+}  // namespace pqb
+
+extern "C" int pq_rotate(const float* X, int64_t nq, int d, const float* R, float* Y,
+                         void* stream) {
+  using namespace pqb;
+  PQ_CHECK_ARG(d > 0, "d must be positive (got %d)", d);
+  PQ_CHECK_ARG(nq >= 0, "nq must be >= 0");
+  if (nq == 0) return PQ_OK;
+  PQ_CHECK_ARG(X && R && Y, "null pointer argument");
+  const int64_t gy = (nq + kRotTile - 1) / kRotTile;
+  PQ_CHECK_ARG(gy < 65536, "too many queries in one call (%lld)", (long long)nq);
+  dim3 grid((d + kRotTile - 1) / kRotTile, (unsigned)gy);
+  rotate_kernel<<<grid, kRotThreads, 0, (cudaStream_t)stream>>>(X, nq, d, R, Y);
+  PQ_LAUNCH_CHECK("rotate_kernel");
+  return PQ_OK;
+}

@@ -1,0 +1,242 @@
+"""GPU parity of the ADC scan, two-stage search, batch search and packed-row
+utilities against the CPU oracle (a NumPy restatement of remex/core.py).
+
+Corpora are encoded by the oracle on the CPU and uploaded, so these tests pin
+the search kernels independently of the GPU encode.  Tolerances: scores within
+1e-4 relative; top-k ids identical except where scores tie within that band.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import remex_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-4
+
+
+def unit_rows(rng, n, d):
+    x = rng.standard_normal((n, d)).astype(np.float32)
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    return x
+
+
+def make_case(bits, d=128, n=2000, seed=42, nq=6, data_seed=42):
+    from polarquant_b200 import CompressedVectors, Quantizer
+    pq = Quantizer(d=d, bits=bits, seed=seed)
+    rng = np.random.default_rng(data_seed)
+    corpus = unit_rows(rng, n, d)
+    qs = unit_rows(rng, nq, d)
+    idx, norms = O.encode(corpus, pq.R, pq.boundaries)
+    cv = CompressedVectors(idx, norms, d, bits)
+    return pq, cv, idx, norms, qs
+
+
+def assert_topk(ids, sc, ref_ids, ref_sc):
+    assert len(ids) == len(ref_ids)
+    assert np.all(np.diff(sc) <= 0), "scores must be descending"
+    assert O.topk_equal_up_to_ties(ids, sc, ref_ids, ref_sc, rtol=RTOL), (ids, ref_ids, sc, ref_sc)
+
+
+@pytest.mark.parametrize("bits", [1, 2, 3, 4, 8])
+def test_search_adc_all_precisions(gpu, bits):
+    pq, cv, idx, norms, qs = make_case(bits)
+    for q in qs[:3]:
+        for prec in [None] + list(range(1, bits + 1)):
+            ri, rs = O.search_adc(pq.R, pq.centroids, pq._nested, bits, idx, norms, q, k=50,
+                                  precision=prec)
+            gi, gs = pq.search_adc(cv, q, k=50, precision=prec)
+            assert_topk(gi, gs, ri, rs)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_search_matches_cached(gpu, bits):
+    pq, cv, idx, norms, qs = make_case(bits)
+    for q in qs[:3]:
+        ri, rs = O.search_cached(pq.R, pq.centroids, pq._nested, bits, idx, norms, q, k=10)
+        gi, gs = pq.search(cv, q, k=10)
+        assert_topk(gi, gs, ri, rs)
+    assert cv._x_hat_rot is None
+
+
+@pytest.mark.parametrize("bits,cands,cp", [(8, 200, None), (8, 200, 4), (4, 200, None),
+                                           (4, 500, 1), (2, 100, 1), (3, 300, 2),
+                                           (8, 2000, None), (8, 2048, 4)])
+def test_twostage(gpu, bits, cands, cp):
+    pq, cv, idx, norms, qs = make_case(bits)
+    for q in qs[:3]:
+        ri, rs = O.search_twostage(pq.R, pq.centroids, pq._nested, bits, idx, norms, q, k=10,
+                                   candidates=cands, coarse_precision=cp)
+        gi, gs = pq.search_twostage(cv, q, k=10, candidates=cands, coarse_precision=cp)
+        assert_topk(gi, gs, ri, rs)
+
+
+def test_twostage_candidates_n_equals_search(gpu):
+    pq, cv, idx, norms, qs = make_case(8)
+    for q in qs[:2]:
+        i_full, _ = pq.search(cv, q, k=10)
+        i_ts, _ = pq.search_twostage(cv, q, k=10, candidates=cv.n)
+        np.testing.assert_array_equal(i_full, i_ts)
+
+
+@pytest.mark.parametrize("bits", [1, 4, 8])
+def test_search_batch(gpu, bits):
+    pq, cv, idx, norms, qs = make_case(bits, nq=20)
+    RI, RS = O.search_batch(pq.R, pq.centroids, pq._nested, bits, idx, norms, qs, k=25)
+    GI, GS = pq.search_batch(cv, qs, k=25)
+    assert GI.shape == RI.shape == (20, 25)
+    for a, b, c, e in zip(GI, GS, RI, RS):
+        assert_topk(a, b, c, e)
+
+
+def test_matryoshka_1bit_equals_standalone_1bit(gpu):
+    # remex tests/test_matryoshka.py:197-210: the MSB of an 8-bit code is the 1-bit code.
+    from polarquant_b200 import CompressedVectors, Quantizer
+    rng = np.random.default_rng(42)
+    corpus = unit_rows(rng, 500, 128)
+    qs = unit_rows(rng, 20, 128)
+    pq8 = Quantizer(128, bits=8, seed=7)
+    pq1 = Quantizer(128, bits=1, seed=7)
+    i8, n8 = O.encode(corpus, pq8.R, pq8.boundaries)
+    i1, n1 = O.encode(corpus, pq1.R, pq1.boundaries)
+    a, _ = pq8.search_batch(CompressedVectors(i8, n8, 128, 8), qs, k=10, precision=1)
+    b, _ = pq1.search_batch(CompressedVectors(i1, n1, 128, 1), qs, k=10)
+    np.testing.assert_array_equal(a, b)
+
+
+def test_packed_vectors_match_compressed(gpu):
+    from polarquant_b200 import PackedVectors
+    pq, cv, idx, norms, qs = make_case(4)
+    pv = PackedVectors.from_compressed(cv)
+    q = qs[0]
+    a = pq.search_adc(cv, q, k=10)
+    b = pq.search_adc(pv, q, k=10)
+    np.testing.assert_array_equal(a[0], b[0])
+    np.testing.assert_allclose(a[1], b[1], rtol=1e-6)
+    a = pq.search_twostage(cv, q, k=10, candidates=200)
+    b = pq.search_twostage(pv, q, k=10, candidates=200)
+    np.testing.assert_array_equal(a[0], b[0])
+    with pytest.raises(TypeError, match="PackedVectors"):
+        pq.search(pv, q, k=10)
+    with pytest.raises(TypeError, match="PackedVectors"):
+        pq.search_batch(pv, qs, k=10)
+
+
+@pytest.mark.parametrize("n", [1, 5, 7, 255, 257, 4097])
+def test_edge_sizes_and_k_over_n(gpu, n):
+    pq, cv, idx, norms, qs = make_case(4, d=64, n=n)
+    q = qs[0]
+    for k in (1, 10, n, n + 100):
+        ri, rs = O.search_adc(pq.R, pq.centroids, pq._nested, 4, idx, norms, q, k=k)
+        gi, gs = pq.search_adc(cv, q, k=k)
+        assert len(gi) == min(k, n)
+        assert_topk(gi, gs, ri, rs)
+    gi, gs = pq.search_twostage(cv, q, k=3, candidates=max(1, n // 2))
+    ri, rs = O.search_twostage(pq.R, pq.centroids, pq._nested, 4, idx, norms, q, k=3,
+                               candidates=max(1, n // 2))
+    assert_topk(gi, gs, ri, rs)
+
+
+def test_empty_corpus(gpu):
+    from polarquant_b200 import CompressedVectors, Quantizer
+    pq = Quantizer(64, bits=4)
+    cv = CompressedVectors(np.zeros((0, 64), np.uint8), np.zeros(0, np.float32), 64, 4)
+    i, s = pq.search_adc(cv, np.ones(64, np.float32), k=5)
+    assert i.shape == (0,) and s.shape == (0,)
+    i, s = pq.search_twostage(cv, np.ones(64, np.float32), k=5)
+    assert i.shape == (0,)
+
+
+def test_precision_errors(gpu):
+    pq, cv, idx, norms, qs = make_case(4, n=100)
+    with pytest.raises(ValueError):
+        pq.search(cv, qs[0], precision=0)
+    with pytest.raises(ValueError):
+        pq.search_adc(cv, qs[0], precision=5)
+    with pytest.raises(ValueError, match="Expected d=128"):
+        pq.search_adc(cv, np.ones(64, np.float32))
+
+
+@pytest.mark.parametrize("bits", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("d", [40, 64, 100, 384])
+def test_packed_row_utilities(gpu, bits, d):
+    from polarquant_b200 import CompressedVectors, PackedVectors
+    rng = np.random.default_rng(bits * 1000 + d)
+    n = 37
+    idx = rng.integers(0, 2 ** bits, size=(n, d), dtype=np.uint8)
+    norms = rng.uniform(0.5, 2, n).astype(np.float32)
+    cv = CompressedVectors(idx, norms, d, bits)
+    pv = PackedVectors.from_compressed(cv)
+    np.testing.assert_array_equal(pv._packed, O.pack_rows(idx, bits))
+    np.testing.assert_array_equal(pv.unpack_rows(0, n), idx)
+    np.testing.assert_array_equal(pv.unpack_rows(3, 9), idx[3:9])
+    sel = np.array([0, 5, n - 1, 2])
+    np.testing.assert_array_equal(pv.unpack_at(sel), idx[sel])
+    # device unpack round trip through the host view of CompressedVectors
+    cv2 = pv.to_compressed()
+    np.testing.assert_array_equal(cv2.indices, idx)
+    np.testing.assert_array_equal(cv2.norms, norms)
+    for t in range(1, bits):
+        if t not in (1, 2, 3, 4):
+            continue
+        lo = pv.at_precision(t)
+        np.testing.assert_array_equal(lo.unpack_rows(0, n), idx >> (bits - t))
+        np.testing.assert_array_equal(lo._packed, O.pack_rows(idx >> (bits - t), t))
+    sub = pv.subset(np.array([4, 1]))
+    np.testing.assert_array_equal(sub.unpack_rows(0, 2), idx[[4, 1]])
+
+
+def test_rotate_matches_f64(gpu):
+    import torch
+    from polarquant_b200 import Quantizer
+    pq = Quantizer(384, bits=4)
+    rng = np.random.default_rng(3)
+    Q = rng.standard_normal((130, 384)).astype(np.float32)
+    dev = torch.device("cuda")
+    Y = pq._rotate(Q, dev).cpu().numpy()
+    ref = (Q.astype(np.float64) @ pq.R.astype(np.float64).T)
+    np.testing.assert_allclose(Y, ref, rtol=1e-6, atol=1e-6 * np.abs(ref).max())
+
+
+def test_topk_merge_kernel(gpu):
+    import ctypes
+    import torch
+    from polarquant_b200 import _lib
+    from polarquant_b200.device import ptr, stream_ptr
+    rng = np.random.default_rng(0)
+    parts, nq, kin, k = 4, 3, 50, 37
+    s = rng.standard_normal((parts, nq, kin)).astype(np.float32)
+    s[1, 0, :5] = s[0, 0, :5]  # exact ties across parts
+    ids = (np.arange(parts * nq * kin).reshape(parts, nq, kin)).astype(np.int64)
+    ids[2, 1, 10:] = -1  # unused slots
+    dev = torch.device("cuda")
+    ts, ti = torch.from_numpy(s).to(dev), torch.from_numpy(ids).to(dev)
+    os_, oi = torch.empty((nq, k), device=dev), torch.empty((nq, k), dtype=torch.int64,
+                                                            device=dev)
+    _lib.call("pq_topk_merge", ptr(ts), ptr(ti), parts, nq, kin, k, ptr(os_), ptr(oi),
+              stream_ptr(dev))
+    gs, gi = os_.cpu().numpy(), oi.cpu().numpy()
+    for q in range(nq):
+        sc = s[:, q, :].ravel()
+        idq = ids[:, q, :].ravel()
+        keep = idq >= 0
+        order = np.lexsort((idq[keep], -sc[keep]))[:k]
+        np.testing.assert_array_equal(gi[q], idq[keep][order])
+        np.testing.assert_array_equal(gs[q], sc[keep][order])
+
+
+def test_config1_shape_parity(gpu):
+    """d=384, 4-bit, 10k unit rows (seed 42), 200 queries (seed 99), k=10."""
+    from polarquant_b200 import CompressedVectors, Quantizer
+    pq = Quantizer(384, bits=4, seed=42)
+    corpus = unit_rows(np.random.default_rng(42), 10000, 384)
+    qs = unit_rows(np.random.default_rng(99), 200, 384)
+    idx, norms = O.encode(corpus, pq.R, pq.boundaries)
+    cv = CompressedVectors(idx, norms, 384, 4)
+    GI, GS = pq.search_adc_many(cv, qs, k=10)
+    bad = 0
+    for i in range(200):
+        ri, rs = O.search_adc(pq.R, pq.centroids, pq._nested, 4, idx, norms, qs[i], k=10)
+        bad += not O.topk_equal_up_to_ties(GI[i], GS[i], ri, rs, rtol=RTOL)
+    assert bad == 0
