@@ -56,8 +56,37 @@ const char* pq_last_error(void);
  * *code = 0 when none.  Returns PQ_ERR_CUDA if the synchronisation fails. */
 int pq_device_status(int* code);
 
+/* Number of kernels the library has launched in this process (all devices). */
+int64_t pq_launch_count(void);
+
 /* Packed bytes of one row of d codes at `bits` (remex/packing.py:130-150). */
 int64_t pq_row_bytes(int d, int bits);
+
+/* ---------------------------------------------------------------------------
+ * Encode.  Replaces Quantizer.encode (remex/core.py:484-511) followed by the
+ * row packing of PackedVectors.from_compressed (remex/core.py:203-223):
+ *   norms = f32(sqrt(sum_f64(x^2)));  x_unit = x / max(norms, 1e-8)  (f32)
+ *   codes = searchsorted(boundaries, x_unit @ R^T)   (side='left')
+ *   packed rows (stride ldb) of the MSB-first code stream.
+ * `planes` is the rotation prepared once per (R, d) by pq_prepare_rotation
+ * (R * 2^14 split into fp16 hi/lo planes, pq_rotation_planes_bytes(d) bytes);
+ * R itself (d x d f32) is read for the exact recomputation of coordinates
+ * that land within 1e-6 of a boundary.
+ * X: n x d f32 row-major; norms: n f32 out; boundaries: 2^bits - 1 f32.
+ * Workspace: pq_encode_workspace_bytes(n, d) (rows are processed in chunks).
+ * ------------------------------------------------------------------------- */
+size_t pq_rotation_planes_bytes(int d);
+int pq_prepare_rotation(const float* R, int d, void* planes, size_t planes_bytes, void* stream);
+size_t pq_encode_workspace_bytes(int64_t n, int d);
+int pq_encode(const float* X, int64_t n, int d, const float* R, const void* planes,
+              const float* boundaries, int bits, uint8_t* packed, int64_t ldb, float* norms,
+              void* ws, size_t ws_bytes, void* stream);
+
+/* Tensor-core rotation Y = X @ R^T (f32) through the encode GEMM, for large
+ * row counts (same workspace as pq_encode).  Used by decode (X_hat_rot @ R,
+ * remex/core.py:531) with the planes of R^T. */
+int pq_rotate_tc(const float* X, int64_t n, int d, const void* planes, float* Y, void* ws,
+                 size_t ws_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Query rotation: Y = X @ R^T (nq x d, f32), i.e. q_rot = R @ q per query.
@@ -66,6 +95,16 @@ int64_t pq_row_bytes(int d, int bits);
  * accumulated in f64, rounded once to f32.
  * ------------------------------------------------------------------------- */
 int pq_rotate(const float* X, int64_t nq, int d, const float* R, float* Y, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Decode (remex/core.py:513-532): out = (cent[codes >> (bits-precision)] @ R)
+ * * norms, n x d f32.  RT is R transposed (d x d f32, device); cent holds the
+ * 2^precision centroids.  Workspace: pq_decode_workspace_bytes(n, d).
+ * ------------------------------------------------------------------------- */
+size_t pq_decode_workspace_bytes(int64_t n, int d);
+int pq_decode(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d, int bits,
+              int precision, const float* cent, const float* RT, float* out, void* ws,
+              size_t ws_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * ADC scan + top-k.  Replaces, per query,
@@ -103,8 +142,10 @@ int pq_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
 
 /* ---------------------------------------------------------------------------
  * Full-precision rescoring of given rows + top-k (stage 2 of
- * remex/core.py:706-719 and remex/ivf.py:422-436).  cand: nq x C local row
- * ids (entries < 0 are skipped).  Output ids are row + row_offset.
+ * remex/core.py:706-719 and remex/ivf.py:422-436).  cand: nq x C global row
+ * ids; the local row is id - row_offset and ids outside this shard's
+ * [row_offset, row_offset + n) (or < 0) are skipped, so a row-sharded corpus
+ * reranks each candidate on the rank that owns it.  Output ids are global.
  * ------------------------------------------------------------------------- */
 int pq_rerank(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
               int bits, const float* qrot, int nq, const float* cent_full, const int64_t* cand,

@@ -27,7 +27,15 @@ SIGNATURES = {
     "pq_last_error": (ctypes.c_char_p, []),
     "pq_device_status": (_I, [ctypes.POINTER(_I)]),
     "pq_row_bytes": (_L, [_I, _I]),
+    "pq_launch_count": (_L, []),
     "pq_rotate": (_I, [_P, _L, _I, _P, _P, _P]),
+    "pq_rotation_planes_bytes": (_Z, [_I]),
+    "pq_prepare_rotation": (_I, [_P, _I, _P, _Z, _P]),
+    "pq_encode_workspace_bytes": (_Z, [_L, _I]),
+    "pq_encode": (_I, [_P, _L, _I, _P, _P, _P, _I, _P, _L, _P, _P, _Z, _P]),
+    "pq_rotate_tc": (_I, [_P, _L, _I, _P, _P, _P, _Z, _P]),
+    "pq_decode_workspace_bytes": (_Z, [_L, _I]),
+    "pq_decode": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _P, _P, _P, _Z, _P]),
     "pq_adc_scan_workspace_bytes": (_Z, [_L, _I, _I]),
     "pq_adc_scan": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _I, _P, _I, _L, _P, _P, _P, _Z, _P]),
     "pq_twostage_workspace_bytes": (_Z, [_L, _I, _I]),

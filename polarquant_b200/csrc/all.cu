@@ -4,3 +4,4 @@
 #include "scan.cu"
 #include "rotate.cu"
 #include "sort.cu"
+#include "encode.cu"

@@ -8,6 +8,7 @@ namespace pqb {
 
 
 static thread_local char t_err[512] = "";
+long long g_launches = 0;
 
 void set_error(const char* fmt, ...) {
   va_list ap;
@@ -49,6 +50,8 @@ int pq_device_status(int* code) {
   }
   return PQ_OK;
 }
+
+int64_t pq_launch_count(void) { return __atomic_load_n(&pqb::g_launches, __ATOMIC_RELAXED); }
 
 int64_t pq_row_bytes(int d, int bits) {
   if (d < 0 || !pqb::supported_bits(bits)) return -1;

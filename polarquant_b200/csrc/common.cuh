@@ -28,8 +28,13 @@ int fail(int code, const char* fmt, ...);
       return ::pqb::fail(PQ_ERR_CUDA, "%s failed: %s", #expr, cudaGetErrorString(_e)); \
   } while (0)
 
+// Every kernel launch of the library is followed by PQ_LAUNCH_CHECK, which
+// also counts it (pq_launch_count()).
+extern long long g_launches;
+
 #define PQ_LAUNCH_CHECK(what)                                                       \
   do {                                                                              \
+    __atomic_fetch_add(&::pqb::g_launches, 1, __ATOMIC_RELAXED);                    \
     cudaError_t _e = cudaGetLastError();                                            \
     if (_e != cudaSuccess)                                                          \
       return ::pqb::fail(PQ_ERR_CUDA, "launch of %s failed: %s", what, cudaGetErrorString(_e)); \

@@ -121,7 +121,11 @@ rerank_kernel(const uint8_t* __restrict__ packed, int64_t ldb, const float* __re
     nrows = *tk.count;
     for (int i = threadIdx.x; i < nrows; i += blockDim.x) rows[i] = tk.id[i];
   } else {
-    for (int i = threadIdx.x; i < C; i += blockDim.x) rows[i] = cand[(size_t)q * C + i];
+    // Candidate ids are global; rows owned by this shard map to [0, n).
+    for (int i = threadIdx.x; i < C; i += blockDim.x) {
+      const long long g = cand[(size_t)q * C + i];
+      rows[i] = (g < 0) ? -1 : g - id_offset;
+    }
     nrows = C;
   }
   build_query_state<B>(qrot + (size_t)q * d, d, cent_full, st, st, st + d);
