@@ -119,11 +119,25 @@ int pq_decode(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n,
  * reference's full-argsort case) takes a sort-based path one query at a time.
  * Output: nq x k, ids are row + row_offset.
  * ------------------------------------------------------------------------- */
-size_t pq_adc_scan_workspace_bytes(int64_t n, int nq, int k);
+size_t pq_adc_scan_workspace_bytes(int64_t n, int d, int nq, int k);
 int pq_adc_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
                 int bits, int precision, const float* qrot, int nq, const float* cent, int k,
                 int64_t row_offset, float* out_scores, int64_t* out_ids, void* ws,
                 size_t ws_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Batched ADC on the tensor cores (tcgen05): scores of nq queries against
+ * all n rows as one GEMM over decoded code tiles (fp16 hi/lo split, three
+ * MMAs per K step, f32 accumulation), with the exact per-query top-k fused in
+ * the epilogue.  Replaces Quantizer.search_batch (remex/core.py:721-778:
+ * `Q_rot @ X_hat_rot.T * norms` and the per-row argpartition/argsort).
+ * Same arguments and output as pq_adc_scan; 1 <= k <= 256, k <= n.
+ * ------------------------------------------------------------------------- */
+size_t pq_adc_batch_workspace_bytes(int64_t n, int d, int nq, int k);
+int pq_adc_batch(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
+                 int bits, int precision, const float* qrot, int nq, const float* cent, int k,
+                 int64_t row_offset, float* out_scores, int64_t* out_ids, void* ws,
+                 size_t ws_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Two-stage Matryoshka search.  Replaces Quantizer.search_twostage
@@ -132,8 +146,10 @@ int pq_adc_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
  * sum_j q_rot[j]*cent_full[code_j]*norm of those rows, top-k.
  * candidates <= PQ_TOPK_MAX, candidates <= n, k <= candidates.
  * cent_coarse: 2^coarse_precision centroids; cent_full: 2^bits centroids.
+ * Batches of >= 64 queries with candidates <= 256 run the coarse stage on the
+ * tensor cores (as pq_adc_batch); smaller batches use the streaming scan.
  * ------------------------------------------------------------------------- */
-size_t pq_twostage_workspace_bytes(int64_t n, int nq, int candidates);
+size_t pq_twostage_workspace_bytes(int64_t n, int d, int nq, int candidates);
 int pq_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
                 int bits, int coarse_precision, const float* qrot, int nq,
                 const float* cent_coarse, const float* cent_full, int candidates, int k,

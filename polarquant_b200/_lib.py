@@ -36,9 +36,11 @@ SIGNATURES = {
     "pq_rotate_tc": (_I, [_P, _L, _I, _P, _P, _P, _Z, _P]),
     "pq_decode_workspace_bytes": (_Z, [_L, _I]),
     "pq_decode": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _P, _P, _P, _Z, _P]),
-    "pq_adc_scan_workspace_bytes": (_Z, [_L, _I, _I]),
+    "pq_adc_scan_workspace_bytes": (_Z, [_L, _I, _I, _I]),
+    "pq_adc_batch_workspace_bytes": (_Z, [_L, _I, _I, _I]),
+    "pq_adc_batch": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _I, _P, _I, _L, _P, _P, _P, _Z, _P]),
     "pq_adc_scan": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _I, _P, _I, _L, _P, _P, _P, _Z, _P]),
-    "pq_twostage_workspace_bytes": (_Z, [_L, _I, _I]),
+    "pq_twostage_workspace_bytes": (_Z, [_L, _I, _I, _I]),
     "pq_twostage": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _I, _P, _P, _I, _I, _L, _P, _P, _P,
                          _Z, _P]),
     "pq_rerank": (_I, [_P, _L, _P, _L, _I, _I, _P, _I, _P, _P, _I, _I, _L, _P, _P, _P]),

@@ -32,6 +32,8 @@ from .packing import pack, packed_nbytes, pack_rows, unpack, unpack_rows
 from .params import haar_rotation, lloyd_max_codebook, nested_codebooks
 
 TOPK_MAX = _lib.PQ_TOPK_MAX
+BATCH_MIN = 64       # queries per call from which the tensor-core path is used
+BATCH_MAX_K = 256    # largest k of the tensor-core path
 
 
 # ---------------------------------------------------------------------------
@@ -489,8 +491,13 @@ class Quantizer:
         return float(np.mean(np.sum((Xh - X_hat) ** 2, axis=1)))
 
     # -- search -------------------------------------------------------------
-    def _scan(self, rows: _DeviceRows, qrot: torch.Tensor, k: int, p: int):
-        """Top-min(k, n) ADC results for each row of qrot, on the device."""
+    def _scan(self, rows: _DeviceRows, qrot: torch.Tensor, k: int, p: int,
+              force: Optional[str] = None):
+        """Top-min(k, n) ADC results for each row of qrot, on the device.
+
+        Batches of BATCH_MIN or more queries (k <= BATCH_MAX_K) run on the
+        tensor cores (pq_adc_batch); smaller ones stream the corpus once per
+        query (pq_adc_scan).  `force` ("batch" / "scan") selects a path."""
         dev = rows.device
         nq = qrot.shape[0]
         K = min(int(k), rows.n)
@@ -498,10 +505,12 @@ class Quantizer:
             return (torch.empty((nq, 0), dtype=torch.float32, device=dev),
                     torch.empty((nq, 0), dtype=torch.int64, device=dev))
         cent = self._params(dev).cent[p]
-        ws = workspace(_lib.query("pq_adc_scan_workspace_bytes", rows.n, nq, K), dev)
+        batched = nq >= BATCH_MIN and K <= BATCH_MAX_K if force is None else force == "batch"
+        fn = "pq_adc_batch" if batched else "pq_adc_scan"
+        ws = workspace(_lib.query(fn + "_workspace_bytes", rows.n, rows.d, nq, K), dev)
         out_s = torch.empty((nq, K), dtype=torch.float32, device=dev)
         out_i = torch.empty((nq, K), dtype=torch.int64, device=dev)
-        _lib.call("pq_adc_scan", ptr(rows.buf), rows.ldb, ptr(rows.norms), rows.n, rows.d,
+        _lib.call(fn, ptr(rows.buf), rows.ldb, ptr(rows.norms), rows.n, rows.d,
                   rows.bits, p, ptr(qrot), nq, ptr(cent), K, 0, ptr(out_s), ptr(out_i),
                   ptr(ws), ws.numel(), stream_ptr(dev))
         return out_s, out_i
@@ -521,7 +530,7 @@ class Quantizer:
             raise NotImplementedError(f"candidates={ck} exceeds the fused limit {TOPK_MAX}")
         K = min(int(k), ck)
         pr = self._params(dev)
-        ws = workspace(_lib.query("pq_twostage_workspace_bytes", rows.n, nq, ck), dev)
+        ws = workspace(_lib.query("pq_twostage_workspace_bytes", rows.n, rows.d, nq, ck), dev)
         out_s = torch.empty((nq, K), dtype=torch.float32, device=dev)
         out_i = torch.empty((nq, K), dtype=torch.int64, device=dev)
         _lib.call("pq_twostage", ptr(rows.buf), rows.ldb, ptr(rows.norms), rows.n, rows.d,

@@ -5,3 +5,4 @@
 #include "rotate.cu"
 #include "sort.cu"
 #include "encode.cu"
+#include "batched.cu"

@@ -296,6 +296,11 @@ static int run_scan(const uint8_t* packed, int64_t ldb, const float* norms, int6
   return PQ_OK;
 }
 
+static int run_batched(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
+                       int bits, int precision, const float* qrot, int nq, const float* cent, int K,
+                       int64_t row_offset, void* ws, size_t ws_bytes, cudaStream_t st,
+                       float** parts_s, long long** parts_id, int* nparts);
+
 static int adc_large_k(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
                        int bits, int precision, const float* qrot, int nq, const float* cent,
                        int k, int64_t row_offset, float* out_s, int64_t* out_ids, void* ws,
@@ -303,7 +308,8 @@ static int adc_large_k(const uint8_t* packed, int64_t ldb, const float* norms, i
 
 extern "C" {
 
-size_t pq_adc_scan_workspace_bytes(int64_t n, int nq, int k) {
+size_t pq_adc_scan_workspace_bytes(int64_t n, int d, int nq, int k) {
+  (void)d;
   if (n <= 0 || nq <= 0 || k <= 0) return 256;
   if (k > PQ_TOPK_MAX) {
     size_t p = 2048;
@@ -328,7 +334,7 @@ int pq_adc_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
   PQ_CHECK_ARG(n < (1ll << 31), "n=%lld rows exceed one launch; shard the corpus", (long long)n);
   if (nq == 0) return PQ_OK;
   PQ_CHECK_ARG(qrot && cent && out_scores && out_ids, "null pointer argument");
-  const size_t need = pq_adc_scan_workspace_bytes(n, nq, k);
+  const size_t need = pq_adc_scan_workspace_bytes(n, d, nq, k);
   if (ws_bytes < need || !ws)
     return fail(PQ_ERR_WORKSPACE, "pq_adc_scan needs %zu workspace bytes, got %zu", need, ws_bytes);
   cudaStream_t st = (cudaStream_t)stream;
@@ -346,8 +352,19 @@ int pq_adc_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
                       (long long*)out_ids, st);
 }
 
-size_t pq_twostage_workspace_bytes(int64_t n, int nq, int candidates) {
-  return pq_adc_scan_workspace_bytes(n, nq, candidates);
+// Query batches at least this large run the coarse stage of two-stage search
+// on the tensor cores (batched ADC); smaller ones use the streaming scan.
+constexpr int kTwostageBatchMin = 64;
+
+static size_t batched_ws(int64_t n, int d, int nq, int k);
+
+size_t pq_twostage_workspace_bytes(int64_t n, int d, int nq, int candidates) {
+  const size_t a = pq_adc_scan_workspace_bytes(n, d, nq, candidates);
+  if (nq >= kTwostageBatchMin && candidates <= 256) {
+    const size_t b = batched_ws(n, d, nq, candidates);
+    return a > b ? a : b;
+  }
+  return a;
 }
 
 static size_t rerank_smem(int d, int bits, int C, int K) {
@@ -369,17 +386,25 @@ int pq_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
   PQ_CHECK_ARG(k >= 1 && k <= candidates, "k must be in [1, candidates] (got %d)", k);
   if (nq == 0) return PQ_OK;
   PQ_CHECK_ARG(qrot && cent_coarse && cent_full && out_scores && out_ids, "null pointer argument");
-  const size_t need = pq_twostage_workspace_bytes(n, nq, candidates);
+  const size_t need = pq_twostage_workspace_bytes(n, d, nq, candidates);
   if (ws_bytes < need || !ws)
     return fail(PQ_ERR_WORKSPACE, "pq_twostage needs %zu workspace bytes, got %zu", need, ws_bytes);
   cudaStream_t st = (cudaStream_t)stream;
-  const int nblk = scan_blocks(n, nq);
-  Carve cv(ws, ws_bytes);
-  const size_t c = (size_t)nq * nblk * candidates;
-  float* cs = cv.take<float>(c);
-  long long* ci = cv.take<long long>(c);
-  rc = run_scan(packed, ldb, norms, n, d, bits, coarse_precision, qrot, nq, cent_coarse,
-                candidates, cs, ci, st);
+  float* cs;
+  long long* ci;
+  int nblk;
+  if (nq >= kTwostageBatchMin && candidates <= 256) {
+    rc = run_batched(packed, ldb, norms, n, d, bits, coarse_precision, qrot, nq, cent_coarse,
+                     candidates, 0, ws, ws_bytes, st, &cs, &ci, &nblk);
+  } else {
+    nblk = scan_blocks(n, nq);
+    Carve cv(ws, ws_bytes);
+    const size_t c = (size_t)nq * nblk * candidates;
+    cs = cv.take<float>(c);
+    ci = cv.take<long long>(c);
+    rc = run_scan(packed, ldb, norms, n, d, bits, coarse_precision, qrot, nq, cent_coarse,
+                  candidates, cs, ci, st);
+  }
   if (rc) return rc;
   const size_t sm = rerank_smem(d, bits, candidates, k);
   PQ_DISPATCH_B(bits, {

@@ -240,3 +240,65 @@ def test_config1_shape_parity(gpu):
         ri, rs = O.search_adc(pq.R, pq.centroids, pq._nested, 4, idx, norms, qs[i], k=10)
         bad += not O.topk_equal_up_to_ties(GI[i], GS[i], ri, rs, rtol=RTOL)
     assert bad == 0
+
+
+# ---------------------------------------------------------------------------
+# Tensor-core batched ADC (pq_adc_batch) and the batched coarse stage
+# ---------------------------------------------------------------------------
+
+def _batched(pq, cv, qs, k, prec, force):
+    import torch
+    rows = cv._device()
+    qrot = pq._rotate(qs, rows.device)
+    s, i = pq._scan(rows, qrot, k, pq._level(prec), force=force)
+    return i.cpu().numpy(), s.cpu().numpy()
+
+
+@pytest.mark.parametrize("bits", [1, 2, 3, 4, 8])
+def test_batched_adc_all_precisions(gpu, bits):
+    pq, cv, idx, norms, qs = make_case(bits, d=128, n=3000, nq=70)
+    for prec in [None] + list(range(1, bits)):
+        GI, GS = _batched(pq, cv, qs, 50, prec, "batch")
+        SI, SS = _batched(pq, cv, qs, 50, prec, "scan")
+        bad = 0
+        for q in range(len(qs)):
+            ri, rs = O.search_adc(pq.R, pq.centroids, pq._nested, bits, idx, norms, qs[q], k=50,
+                                  precision=prec)
+            bad += not O.topk_equal_up_to_ties(GI[q], GS[q], ri, rs, rtol=RTOL)
+            assert np.all(np.diff(GS[q]) <= 0)
+            np.testing.assert_allclose(GS[q], SS[q], rtol=RTOL, atol=RTOL * np.abs(SS[q]).max())
+        assert bad == 0, f"{bad} queries differ at precision {prec}"
+
+
+@pytest.mark.parametrize("d,n,nq,k", [(40, 77, 65, 7), (100, 1000, 130, 256), (384, 257, 64, 1),
+                                      (1536, 20000, 200, 100), (768, 5000, 129, 200)])
+def test_batched_adc_shapes(gpu, d, n, nq, k):
+    pq, cv, idx, norms, qs = make_case(4 if d != 768 else 8, d=d, n=n, nq=nq)
+    K = min(k, n)
+    GI, GS = _batched(pq, cv, qs, K, None, "batch")
+    assert GI.shape == (nq, K)
+    bad = 0
+    for q in range(nq):
+        ri, rs = O.search_adc(pq.R, pq.centroids, pq._nested, pq.bits, idx, norms, qs[q], k=K)
+        bad += not O.topk_equal_up_to_ties(GI[q], GS[q], ri, rs, rtol=RTOL)
+    assert bad == 0
+
+
+def test_search_batch_uses_tensor_cores_and_matches(gpu):
+    pq, cv, idx, norms, qs = make_case(4, d=256, n=4000, nq=100)
+    RI, RS = O.search_batch(pq.R, pq.centroids, pq._nested, 4, idx, norms, qs, k=100)
+    GI, GS = pq.search_batch(cv, qs, k=100)
+    for a, b, c, e in zip(GI, GS, RI, RS):
+        assert_topk(a, b, c, e)
+
+
+@pytest.mark.parametrize("bits,cands,cp", [(8, 200, 4), (4, 100, 2), (8, 256, None)])
+def test_twostage_batched_coarse(gpu, bits, cands, cp):
+    pq, cv, idx, norms, qs = make_case(bits, d=128, n=5000, nq=80)
+    GI, GS = pq.search_twostage_many(cv, qs, k=10, candidates=cands, coarse_precision=cp)
+    bad = 0
+    for q in range(len(qs)):
+        ri, rs = O.search_twostage(pq.R, pq.centroids, pq._nested, bits, idx, norms, qs[q], k=10,
+                                   candidates=cands, coarse_precision=cp)
+        bad += not O.topk_equal_up_to_ties(GI[q], GS[q], ri, rs, rtol=RTOL)
+    assert bad == 0
