@@ -48,6 +48,10 @@ WORKLOADS = {
     "c1": dict(d=384, bits=4, n=10_000, nq=200, n_centres=0, sigma=0.0, k=10,
                candidates=0, coarse_precision=None, mode="adc",
                name="search_adc d=384 bits=4 n=10k N(0,1) unit q=200 k=10"),
+    "c4": dict(d=1536, bits=4, n=100_000_000, nq=10_000, n_centres=10_000, sigma=0.2, k=100,
+               candidates=0, coarse_precision=None, mode="batch",
+               name="batched ADC d=1536 bits=4 n=100M clustered(10000, 0.2/sqrt(d)) q=10000 "
+                    "k=100"),
 }
 
 CHUNK = 65536
@@ -176,6 +180,11 @@ def cpu_baseline(cfg, X_sample, Q_host, pq, budget_s=20.0):
             O.search_twostage(pq.R, pq.centroids, pq._nested, cfg["bits"], codes, norms, q,
                               k=cfg["k"], candidates=cfg["candidates"],
                               coarse_precision=cfg["coarse_precision"])
+        elif cfg["mode"] == "batch":
+            # search_batch over a block of 64 queries at a time (remex/core.py:721-778)
+            O.search_batch(pq.R, pq.centroids, pq._nested, cfg["bits"], codes, norms,
+                           Q_host[nq_done:nq_done + 64], k=cfg["k"])
+            nq_done += 63
         else:
             O.search_adc(pq.R, pq.centroids, pq._nested, cfg["bits"], codes, norms, q,
                          k=cfg["k"])
@@ -247,25 +256,50 @@ def main():
             dist.destroy_process_group()
         return
 
-    # ---- build this rank's shard -----------------------------------------
+    # ---- build this rank's shard (generated and encoded chunk by chunk) ---
+    from polarquant_b200.core import CompressedVectors
+    from polarquant_b200.encode import alloc_corpus, encode_into
     r0, r1 = shard_bounds(cfg["n"], world, rank)
-    X = gen_rows(torch, dev, cfg, r0, r1, seed=1, centres=centres)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    cv = pq.encode(X)
-    e1.record()
-    torch.cuda.synchronize()
-    enc_ms = e0.elapsed_time(e1)
+    rows = alloc_corpus(pq, r1 - r0, dev)
+    enc_ms = 0.0
+    step_rows = 1 << 20
+    for a in range(r0, r1, step_rows):
+        b = min(r1, a + step_rows)
+        X = gen_rows(torch, dev, cfg, a, b, seed=1, centres=centres)
+        if a == r0:
+            encode_into(pq, X[: min(len(X), 4096)], rows, 0)  # warm the encode path
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        encode_into(pq, X, rows, a - r0)
+        e1.record()
+        torch.cuda.synchronize()
+        enc_ms += e0.elapsed_time(e1)
+        del X
     enc_vps = (r1 - r0) / (enc_ms / 1e3)
-    del X
+    cv = CompressedVectors._from_device(rows)
     ss = ShardedSearch(pq, cv, r0, cfg["n"])
+    kern_ms = []
+    _local_topk = ss.local_topk
+
+    def timed_local_topk(qrot, k, p):
+        a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_.record()
+        out = _local_topk(qrot, k, p)
+        b_.record()
+        kern_ms.append((a_, b_))
+        return out
+    ss.local_topk = timed_local_topk
 
     def step(Qin):
         if cfg["mode"] == "twostage":
             return ss.search_twostage_many(Qin, k=cfg["k"], candidates=cfg["candidates"],
                                            coarse_precision=cfg["coarse_precision"])
         return ss.search_adc_many(Qin, k=cfg["k"])
+
+    qrot0 = pq._rotate(Q, dev)
+    p_scan = cfg["coarse_precision"] or cfg["bits"]
+    k_scan = min(cfg["candidates"] or cfg["k"], rows.n)
+    batched = cfg["nq"] >= 64 and k_scan <= 256
 
     def barrier():
         if world > 1:
@@ -275,6 +309,7 @@ def main():
     for _ in range(max(3, args.warmup)):
         step(Q)
     barrier()
+    kern_ms.clear()
     launches0 = _lib.query("pq_launch_count")
     clk = ClockSampler(dev.index)
     clk.start()
@@ -288,6 +323,7 @@ def main():
     clocks = clk.stop()
     ms = t0.elapsed_time(t1) / args.steps
     launches = _lib.query("pq_launch_count") - launches0
+    kms = sum(a_.elapsed_time(b_) for a_, b_ in kern_ms) / max(1, len(kern_ms))
     ms_t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
@@ -314,26 +350,44 @@ def main():
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     e2e_ms = float(e2e_t.item())
 
-    # ---- dominant kernel: the per-rank ADC scan, timed alone ---------------
-    rows = cv._device()
-    qrot = pq._rotate(Q, dev)
-    p = cfg["coarse_precision"] or cfg["bits"]
-    kk = min(cfg["candidates"] or cfg["k"], rows.n)
-    for _ in range(2):
-        pq._scan(rows, qrot, kk, p)
+    # ---- dominant kernel ----------------------------------------------------
+    # Batches of >= 64 queries run the per-rank ADC on the tensor cores
+    # (batched_adc_kernel, timed inside the steps above): bound = tensor,
+    # algorithmic work 2*nq*n_local*d flops per launch (each MAC counted once;
+    # the fp16 split issues three MMAs per MAC).
+    hbm, bf16, peak_kind = measured_peaks()
+    row_bytes = rows.row_bytes + 4
+    if batched:
+        flops = 2.0 * cfg["nq"] * rows.n * cfg["d"]
+        ach = flops / (kms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": ach, "peak": bf16, "unit": "TFLOP/s",
+                "frac": ach / bf16, "traffic": None,
+                "kernel": "batched_adc_kernel (tcgen05, fp16 hi/lo split: 3 MMAs per MAC)",
+                "peak_kind": f"{peak_kind} dense bf16 (burst)",
+                "alg_flops_per_launch": flops, "launch_ms": kms}
+    # The streaming single-query scan (pq_adc_scan) on the same corpus: HBM-bound.
+    nsq = 8 if rows.n > 5_000_000 else min(64, cfg["nq"])
+    qs8 = qrot0[:nsq].contiguous()
+    pq._scan(rows, qs8, k_scan, p_scan, force="scan")
     torch.cuda.synchronize()
     k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = max(3, args.steps)
+    reps = 3
     k0.record()
     for _ in range(reps):
-        pq._scan(rows, qrot, kk, p)
+        pq._scan(rows, qs8, k_scan, p_scan, force="scan")
     k1.record()
     torch.cuda.synchronize()
-    kms = k0.elapsed_time(k1) / reps
-    row_bytes = rows.row_bytes + 4
+    sms = k0.elapsed_time(k1) / reps
+    sbytes = nsq * rows.n * row_bytes
+    sgbs = sbytes / (sms / 1e3) / 1e9
+    scan_roof = {"bound": "hbm", "achieved": sgbs, "peak": hbm, "unit": "GB/s",
+                 "frac": sgbs / hbm, "queries_per_launch": nsq, "launch_ms": sms,
+                 "kernel": "scan_topk_kernel (+ merge), one corpus pass per query",
+                 "peak_kind": peak_kind, "alg_bytes_per_launch": sbytes}
+    if not batched:
+        roof = dict(scan_roof, traffic=None)
+        kms = sms
     alg_bytes = cfg["nq"] * rows.n * row_bytes
-    hbm, _, peak_kind = measured_peaks()
-    achieved = alg_bytes / (kms / 1e3) / 1e9
 
     line = {
         "metric": "queries/s", "value": qps, "unit": "queries/s", "n_gpus": world,
@@ -344,12 +398,9 @@ def main():
                    "corpus_rows": cfg["n"], "parallelism": f"row-shard x{world}",
                    "l2": "corpus larger than L2 (no flush needed)"
                    if cfg["n"] * row_bytes > 126e6 else "corpus L2-resident"},
-        "scan_gbs": alg_bytes / (kms / 1e3) / 1e9,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                     "frac": achieved / hbm, "traffic": None,
-                     "kernel": "scan_topk_kernel (+ merge), per-rank coarse scan",
-                     "peak_kind": peak_kind, "alg_bytes_per_launch": alg_bytes,
-                     "launch_ms": kms},
+        "scan_gbs": alg_bytes / (ms / 1e3) / 1e9,
+        "roofline": roof,
+        "scan_roofline": scan_roof,
         "encode": {"vectors_per_s": enc_vps * world, "ms": enc_ms, "rows_per_rank": r1 - r0},
         "e2e": {"value": cfg["nq"] / (e2e_ms / 1e3), "unit": "queries/s",
                 "h2d_bytes_per_step": int(Q.numel() * 4), "d2h_bytes_per_step": int(d2h)},

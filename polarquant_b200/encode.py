@@ -2,6 +2,8 @@
 
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import torch
 
@@ -77,3 +79,33 @@ def rotate_tc(q, X) -> torch.Tensor:
         _lib.call("pq_rotate_tc", ptr(Xd), n, q.d, ptr(_planes(q, dev)), ptr(Y), ptr(ws),
                   ws.numel(), stream_ptr(dev))
     return Y
+
+
+def alloc_corpus(q, n: int, dev):
+    """An uninitialised device corpus of n rows for this quantizer (filled by encode_into)."""
+    from .core import _DeviceRows
+    ldb = row_stride(q.d, q.bits)
+    buf = alloc_rows(n, ldb, dev)
+    norms = torch.empty(int(n), dtype=torch.float32, device=dev)
+    return _DeviceRows(buf, norms, int(n), q.d, q.bits, ldb, dev)
+
+
+def encode_into(q, X, rows, start: int) -> None:
+    """Encodes X (device f32, m x d) into rows [start, start + m) of an existing
+    device corpus, so corpora larger than one f32 staging buffer are built chunk
+    by chunk."""
+    Xd = to_device_f32(X, rows.device)
+    m = Xd.shape[0]
+    if Xd.dim() != 2 or Xd.shape[1] != q.d:
+        raise ValueError(f"Expected d={q.d}")
+    if start < 0 or start + m > rows.n:
+        raise IndexError("rows out of range")
+    if m == 0:
+        return
+    dev = rows.device
+    pr = q._params(dev)
+    ws = workspace(_lib.query("pq_encode_workspace_bytes", m, q.d), dev)
+    pk = ctypes.c_void_p(rows.buf.data_ptr() + int(start) * rows.ldb)
+    nr = ctypes.c_void_p(rows.norms.data_ptr() + int(start) * 4)
+    _lib.call("pq_encode", ptr(Xd), m, q.d, ptr(pr.R), ptr(_planes(q, dev)), ptr(pr.boundaries),
+              q.bits, pk, rows.ldb, nr, ptr(ws), ws.numel(), stream_ptr(dev))
