@@ -140,6 +140,27 @@ int pq_adc_batch(const uint8_t* packed, int64_t ldb, const float* norms, int64_t
                  size_t ws_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Allocation-free variant of pq_adc_scan.  No counterpart in the reference:
+ * it exists for callers that cannot allocate device memory -- hosts that
+ * reserve the GPU's memory for their own pool up front, and latency-critical
+ * paths that cannot pay for cudaMalloc/cudaFree (which may synchronise the
+ * device).  The caller passes only inputs and outputs; the scan's scratch is
+ * a built-in device array of pq_adc_scan_noalloc_scratch_bytes() (16 MiB)
+ * that every GPU loading the library holds until the process exits.  Calls
+ * needing more scratch (many queries x large k) are rejected with
+ * PQ_ERR_WORKSPACE; k <= PQ_TOPK_MAX.  The first call on each device looks up
+ * the array's device address (cudaGetSymbolAddress) and should come before
+ * any stream capture.  All calls on a device share the array, so calls that
+ * overlap on the GPU race and must be serialised by the caller.  Arguments
+ * and results are those of pq_adc_scan.
+ * ------------------------------------------------------------------------- */
+size_t pq_adc_scan_noalloc_scratch_bytes(void);
+int pq_adc_scan_noalloc(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
+                        int bits, int precision, const float* qrot, int nq, const float* cent,
+                        int k, int64_t row_offset, float* out_scores, int64_t* out_ids,
+                        void* stream);
+
+/* ---------------------------------------------------------------------------
  * Two-stage Matryoshka search.  Replaces Quantizer.search_twostage
  * (remex/core.py:638-719): coarse ADC at `coarse_precision` over all rows,
  * top-`candidates` (unordered, any tie order), then full-precision rescoring

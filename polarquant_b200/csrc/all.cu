@@ -6,3 +6,4 @@
 #include "sort.cu"
 #include "encode.cu"
 #include "batched.cu"
+#include "noalloc.cu"
