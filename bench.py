@@ -52,6 +52,12 @@ WORKLOADS = {
                candidates=0, coarse_precision=None, mode="batch",
                name="batched ADC d=1536 bits=4 n=100M clustered(10000, 0.2/sqrt(d)) q=10000 "
                     "k=100"),
+    # The c4 kernel on a 4M-row slice of the same distribution: small enough
+    # for a full ncu capture (3 GB on the device).
+    "c4s": dict(d=1536, bits=4, n=4_000_000, nq=10_000, n_centres=10_000, sigma=0.2, k=100,
+                candidates=0, coarse_precision=None, mode="batch",
+                name="batched ADC d=1536 bits=4 n=4M clustered(10000, 0.2/sqrt(d)) q=10000 "
+                     "k=100"),
 }
 
 CHUNK = 65536
@@ -210,6 +216,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--quick", action="store_true",
+                    help="timed steps only (no e2e, scan roofline or CPU baseline); for profiling")
     args = ap.parse_args()
     cfg = WORKLOADS[args.workload]
 
@@ -329,6 +337,17 @@ def main():
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms = float(ms_t.item())
     qps = cfg["nq"] / (ms / 1e3)
+
+    if args.quick:
+        if rank == 0:
+            print(json.dumps({"metric": "queries/s", "value": qps, "ms_per_step": ms,
+                              "kernel_ms": kms, "n_gpus": world, "quick": True,
+                              "encode_vectors_per_s": enc_vps * world,
+                              "config": {"workload": cfg["name"]}}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     # ---- end to end through the public API with host buffers ---------------
     Qh = torch.empty(Q.shape, dtype=torch.float32, pin_memory=True)

@@ -34,7 +34,8 @@ constexpr int kBatM = 128;
 constexpr int kBatN = 256;
 constexpr int kBatBK = 64;
 constexpr int kBatStages = 2;
-constexpr int kBatThreads = 320;  // w0 TMA(Q), w1 MMA + TMEM, w2-5 epilogue, w6-9 decoder
+constexpr int kBatDecWarps = 8;
+constexpr int kBatThreads = (6 + kBatDecWarps) * 32;  // w0 TMA(Q), w1 MMA + TMEM, w2-5 epilogue, w6.. decoder
 constexpr int kBatMaxK = 256;
 constexpr int kBatScratch = 512;  // per-warp sort scratch entries (power of two >= 2*kBatMaxK)
 
@@ -90,6 +91,163 @@ __device__ __forceinline__ void load8(const uint8_t* row, int k0, uint32_t (&c)[
     const uint32_t v = ((uint32_t)g[0] << 16) | ((uint32_t)g[1] << 8) | (uint32_t)g[2];
 #pragma unroll
     for (int u = 0; u < 8; ++u) c[u] = (v >> (21 - 3 * u)) & 7u;
+  }
+}
+
+// Decoder geometry for B-bit codes: one K block (64 codes) of a row is RB
+// bytes, read as PER_ROW segments of SEG bytes; every decoder thread owns UPT
+// segments of each stage.
+template <int B>
+struct DecSeg {
+  static constexpr int RB = 8 * B;
+  static constexpr int SEG = (B == 3) ? 24 : (RB < 16 ? RB : 16);
+  static constexpr int PER_ROW = RB / SEG;
+  static constexpr int UPT = kBatN * PER_ROW / (kBatDecWarps * 32);
+  static constexpr int WORDS = SEG / 4;
+  static constexpr int CODES = SEG * 8 / B;
+};
+
+template <int B>
+__device__ __forceinline__ void load_seg(const uint8_t* p, uint32_t (&w)[DecSeg<B>::WORDS]) {
+  if constexpr (DecSeg<B>::SEG == 16) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < DecSeg<B>::WORDS / 2; ++i) {
+      const uint2 v = __ldg(reinterpret_cast<const uint2*>(p) + i);
+      w[2 * i] = v.x;
+      w[2 * i + 1] = v.y;
+    }
+  }
+}
+
+// Code t of a segment (MSB-first stream starting at the segment's first byte).
+template <int B>
+__device__ __forceinline__ uint32_t seg_code(const uint32_t* w, int t) {
+  if constexpr (B == 3) {
+    const int g = t >> 3, u = t & 7;
+    auto byte = [&](int i) { return (w[i >> 2] >> (8 * (i & 3))) & 255u; };
+    const uint32_t v = (byte(3 * g) << 16) | (byte(3 * g + 1) << 8) | byte(3 * g + 2);
+    return (v >> (21 - 3 * u)) & 7u;
+  } else {
+    const int p = t * B;
+    const int byte = p >> 3, sh = 8 - B - (p & 7);
+    return (w[byte >> 2] >> (8 * (byte & 3) + sh)) & ((1u << B) - 1u);
+  }
+}
+
+// The (task, tile, k-block) sequence every role of the batched kernel walks.
+struct BatWalk {
+  int t, tile, kb, tiles;
+  int64_t r0, r1;
+};
+
+__device__ __forceinline__ void walk_task(BatWalk& w, const BatArgs& p) {
+  const int rc = w.t / p.qtiles;
+  w.r0 = (int64_t)rc * p.rows_per_chunk;
+  w.r1 = min(p.n, w.r0 + p.rows_per_chunk);
+  w.tiles = (int)((w.r1 - w.r0 + kBatN - 1) / kBatN);
+}
+
+__device__ __forceinline__ void walk_next(BatWalk& w, const BatArgs& p, int ntasks) {
+  if (++w.kb == p.nk) {
+    w.kb = 0;
+    if (++w.tile == w.tiles) {
+      w.tile = 0;
+      w.t += gridDim.x;
+      if (w.t < ntasks) walk_task(w, p);
+    }
+  }
+}
+
+template <int B>
+__device__ __forceinline__ void dec_load(const BatArgs& p, const BatWalk& w, int dt,
+                                         uint32_t (&seg)[DecSeg<B>::UPT][DecSeg<B>::WORDS]) {
+  using S = DecSeg<B>;
+  const int64_t tr0 = w.r0 + (int64_t)w.tile * kBatN;
+#pragma unroll
+  for (int i = 0; i < S::UPT; ++i) {
+    const int u = dt + i * kBatDecWarps * 32;
+    const int r = u / S::PER_ROW, sg = u % S::PER_ROW;
+    const int64_t row = tr0 + r;
+    if (row < w.r1) {
+      load_seg<B>(p.packed + row * p.ldb + (int64_t)w.kb * S::RB + sg * S::SEG, seg[i]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < S::WORDS; ++j) seg[i][j] = 0xFFFFFFFFu;  // marks a padding row
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t ordered_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Warp-cooperative selection on lane `src`'s candidate buffer (n <= 512
+// entries, appended in increasing row order): finds the K-th largest score by
+// a 32-step radix search on order-preserving keys, then compacts in place to
+// the entries above it plus the earliest (lowest-row) entries equal to it, so
+// exactly K remain.  Lane src receives the new count and threshold.  About a
+// fifth of the cost of sorting the buffer.
+__device__ __forceinline__ void warp_select(int src, int lane, int n_src, float* bs, int* bi, int K,
+                                            int& cnt, float& thr) {
+  __syncwarp();
+  const int n = __shfl_sync(0xffffffffu, n_src, src);
+  if (n <= K) return;
+  constexpr int PER = kBatScratch / 32;  // 16 entries per lane
+  uint32_t key[PER];
+  float sv[PER];
+  int iv[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int e = j * 32 + lane;
+    sv[j] = (e < n) ? bs[e] : -INFINITY;
+    iv[j] = (e < n) ? bi[e] : 0;
+    key[j] = (e < n) ? ordered_key(sv[j]) : 0u;
+  }
+  uint32_t prefix = 0;
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t cand = prefix | (1u << bit);
+    int c = 0;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) c += key[j] >= cand;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    if (c >= K) prefix = cand;
+  }
+  // prefix = K-th largest key.  Keep key > prefix, then ties in buffer order.
+  int above = 0;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) above += key[j] > prefix;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) above += __shfl_xor_sync(0xffffffffu, above, o);
+  int ties_left = K - above;
+  int out = 0;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const bool gt = key[j] > prefix;
+    const bool eq = key[j] == prefix && (j * 32 + lane) < n;
+    const uint32_t eqm = __ballot_sync(0xffffffffu, eq);
+    const int eq_rank = __popc(eqm & ((1u << lane) - 1u));
+    const bool keep = gt || (eq && eq_rank < ties_left);
+    const uint32_t km = __ballot_sync(0xffffffffu, keep);
+    if (keep) {
+      const int pos = out + __popc(km & ((1u << lane) - 1u));
+      bs[pos] = sv[j];
+      bi[pos] = iv[j];
+    }
+    out += __popc(km);
+    ties_left -= min(ties_left, __popc(eqm));
+  }
+  // Scores equal to the threshold arriving later have larger rows: rejected.
+  uint32_t tk = prefix;
+  const float t = __uint_as_float((tk & 0x80000000u) ? (tk & 0x7FFFFFFFu) : ~tk);
+  __syncwarp();
+  if (lane == src) {
+    cnt = K;
+    thr = t;
   }
 }
 
@@ -176,7 +334,7 @@ batched_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_const
   if (threadIdx.x == 0) {
     for (int s = 0; s < kBatStages; ++s) {
       tc::mbar_init(bar(FULLA + s), 1);
-      tc::mbar_init(bar(FULLB + s), 4);
+      tc::mbar_init(bar(FULLB + s), kBatDecWarps);
       tc::mbar_init(bar(EMPTY + s), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -281,55 +439,63 @@ batched_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_const
     }
   } else if (warp >= 6) {
     // ---------------- decoder: corpus tiles ----------------
-    const int dt = threadIdx.x - 6 * 32;  // 0..127
-    int it = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < ntasks && ok; t += gridDim.x) {
-      const int rc = t / p.qtiles;
-      const int64_t r0 = (int64_t)rc * p.rows_per_chunk;
-      const int64_t r1 = min(p.n, r0 + p.rows_per_chunk);
-      const int tiles = (int)((r1 - r0 + kBatN - 1) / kBatN);
-      for (int tile = 0; tile < tiles && ok; ++tile) {
-        const int64_t tr0 = r0 + (int64_t)tile * kBatN;
-        for (int kb = 0; kb < p.nk; ++kb, ++it) {
-          const int s = it % kBatStages;
-          const uint32_t ph = (uint32_t)(it / kBatStages) & 1u;
-          if (!tc::mbar_wait(bar(EMPTY + s), ph ^ 1u, abort_flag, tc::kErrWaitStageEmpty)) {
-            ok = false;
-            break;
-          }
-          uint8_t* xh = gbase + (size_t)s * STAGE + 2 * QPLANE;
-          uint8_t* xl = xh + XPLANE;
-#pragma unroll 4
-          for (int u = dt; u < kBatN * 8; u += 128) {
-            const int r = u >> 3, c = u & 7;
-            const int64_t row = tr0 + r;
-            uint4 vh = make_uint4(0, 0, 0, 0), vl = make_uint4(0, 0, 0, 0);
-            if (row < r1) {
-              uint32_t code[8];
-              load8<B>(p.packed + row * p.ldb, kb * kBatBK + c * 8, code);
-              uint32_t e[8];
+    // Each thread owns UPT row segments per stage.  The segments of the next
+    // stage are loaded into registers before waiting for the current stage's
+    // buffer, so HBM latency overlaps the MMAs of the stages in flight.
+    using S = DecSeg<B>;
+    const int dt = threadIdx.x - 6 * 32;
+    BatWalk w;
+    w.t = blockIdx.x;
+    w.tile = 0;
+    w.kb = 0;
+    if (w.t < ntasks) walk_task(w, p);
+    uint32_t cur[S::UPT][S::WORDS], nxt[S::UPT][S::WORDS];
+    if (w.t < ntasks) dec_load<B>(p, w, dt, cur);
+    for (int it = 0; w.t < ntasks; ++it) {
+      const BatWalk here = w;
+      walk_next(w, p, ntasks);
+      if (w.t < ntasks) dec_load<B>(p, w, dt, nxt);
+      const int s = it % kBatStages;
+      const uint32_t ph = (uint32_t)(it / kBatStages) & 1u;
+      if (!tc::mbar_wait(bar(EMPTY + s), ph ^ 1u, abort_flag, tc::kErrWaitStageEmpty)) break;
+      uint8_t* xh = gbase + (size_t)s * STAGE + 2 * QPLANE;
+      uint8_t* xl = xh + XPLANE;
+      const int64_t tr0 = here.r0 + (int64_t)here.tile * kBatN;
 #pragma unroll
-              for (int t2 = 0; t2 < 8; ++t2) e[t2] = slut[code[t2] >> p.shift];
-              vh.x = __byte_perm(e[0], e[1], 0x5410);
-              vh.y = __byte_perm(e[2], e[3], 0x5410);
-              vh.z = __byte_perm(e[4], e[5], 0x5410);
-              vh.w = __byte_perm(e[6], e[7], 0x5410);
-              vl.x = __byte_perm(e[0], e[1], 0x7632);
-              vl.y = __byte_perm(e[2], e[3], 0x7632);
-              vl.z = __byte_perm(e[4], e[5], 0x7632);
-              vl.w = __byte_perm(e[6], e[7], 0x7632);
-            }
-            const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(c ^ (r & 7)) << 4);
-            *reinterpret_cast<uint4*>(xh + off) = vh;
-            *reinterpret_cast<uint4*>(xl + off) = vl;
+      for (int i = 0; i < S::UPT; ++i) {
+        const int u = dt + i * kBatDecWarps * 32;
+        const int r = u / S::PER_ROW, sg = u % S::PER_ROW;
+        const bool live = tr0 + r < here.r1;
+#pragma unroll
+        for (int cc = 0; cc < S::CODES / 8; ++cc) {
+          uint4 vh = make_uint4(0, 0, 0, 0), vl = make_uint4(0, 0, 0, 0);
+          if (live) {
+            uint32_t e[8];
+#pragma unroll
+            for (int t2 = 0; t2 < 8; ++t2) e[t2] = slut[seg_code<B>(cur[i], cc * 8 + t2) >> p.shift];
+            vh.x = __byte_perm(e[0], e[1], 0x5410);
+            vh.y = __byte_perm(e[2], e[3], 0x5410);
+            vh.z = __byte_perm(e[4], e[5], 0x5410);
+            vh.w = __byte_perm(e[6], e[7], 0x5410);
+            vl.x = __byte_perm(e[0], e[1], 0x7632);
+            vl.y = __byte_perm(e[2], e[3], 0x7632);
+            vl.z = __byte_perm(e[4], e[5], 0x7632);
+            vl.w = __byte_perm(e[6], e[7], 0x7632);
           }
-          // Make the generic-proxy stores visible to the tensor core (async proxy).
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          __syncwarp();
-          if (lane == 0) tc::mbar_arrive(bar(FULLB + s));
+          const int c = sg * (S::CODES / 8) + cc;
+          const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(c ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(xh + off) = vh;
+          *reinterpret_cast<uint4*>(xl + off) = vl;
         }
       }
+      // Make the generic-proxy stores visible to the tensor core (async proxy).
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(bar(FULLB + s));
+#pragma unroll
+      for (int i = 0; i < S::UPT; ++i)
+#pragma unroll
+        for (int j = 0; j < S::WORDS; ++j) cur[i][j] = nxt[i][j];
     }
   } else {
     // ---------------- epilogue: warps 2..5, thread = query ----------------
@@ -374,7 +540,7 @@ batched_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_const
             need &= need - 1;
             float* sbs = p.buf_s + ((size_t)blockIdx.x * kBatM + 32 * (warp & 3) + src) * p.cap;
             int* sbi = p.buf_i + ((size_t)blockIdx.x * kBatM + 32 * (warp & 3) + src) * p.cap;
-            warp_compact(src, lane, cnt, sbs, sbi, p.K, ss, si, cnt, thr, nullptr, nullptr, 0);
+            warp_select(src, lane, cnt, sbs, sbi, p.K, cnt, thr);
           }
           const int64_t rb = tr0 + c0;
           if (qv && rb < r1) {
@@ -455,11 +621,25 @@ static BatPlan bat_plan(int64_t n, int d, int nq, int k) {
   b.nk = b.ldk / kBatBK;
   b.qtiles = (nq + kBatM - 1) / kBatM;
   b.nq_pad = b.qtiles * kBatM;
-  const int target = 8 * num_sms();
-  int rc = (target + b.qtiles - 1) / b.qtiles;
+  // Row chunks per query tile: the smallest count whose task total fills the
+  // SMs in whole waves (>= 97% of the last wave busy), so no SM idles at the
+  // end; tasks stay >= 4 row tiles long.
+  const int sms = num_sms();
   const int64_t min_rows = 4 * kBatN;
-  const int64_t max_rc = (n + min_rows - 1) / min_rows;
-  if (rc > max_rc) rc = (int)(max_rc < 1 ? 1 : max_rc);
+  const int64_t max_rc = (n + min_rows - 1) / min_rows < 1 ? 1 : (n + min_rows - 1) / min_rows;
+  int rc = 1;
+  double best = -1.0;
+  const int lo = (sms + b.qtiles - 1) / b.qtiles;
+  for (int c = lo < 1 ? 1 : lo; c <= 16 * lo + 16 && c <= max_rc; ++c) {
+    const int64_t tasks = (int64_t)c * b.qtiles;
+    const double eff = (double)tasks / (double)(((tasks + sms - 1) / sms) * sms);
+    if (eff > best + 1e-9) {
+      best = eff;
+      rc = c;
+    }
+    if (eff >= 0.97) break;
+  }
+  if (best < 0) rc = (int)(max_rc < lo ? max_rc : lo);
   b.rpc = ((n + rc - 1) / rc + kBatN - 1) / kBatN * kBatN;
   if (b.rpc < kBatN) b.rpc = kBatN;
   b.rchunks = (int)((n + b.rpc - 1) / b.rpc);
