@@ -52,6 +52,10 @@ WORKLOADS = {
                candidates=0, coarse_precision=None, mode="batch",
                name="batched ADC d=1536 bits=4 n=100M clustered(10000, 0.2/sqrt(d)) q=10000 "
                     "k=100"),
+    "c5": dict(d=384, bits=4, n=10_000_000, nq=1000, n_centres=4096, sigma=0.1, k=10,
+               candidates=500, coarse_precision=2, mode="ivf", n_bits=12, nprobe=32,
+               name="IVF lsh n_bits=12 (4096 cells) nprobe=32 d=384 bits=4 n=10M "
+                    "clustered(4096, 0.1/sqrt(d)) q=1000 cp=2 C=500 k=10"),
     # The c4 kernel on a 4M-row slice of the same distribution: small enough
     # for a full ncu capture (3 GB on the device).
     "c4s": dict(d=1536, bits=4, n=4_000_000, nq=10_000, n_centres=10_000, sigma=0.2, k=100,
@@ -186,6 +190,15 @@ def cpu_baseline(cfg, X_sample, Q_host, pq, budget_s=20.0):
             O.search_twostage(pq.R, pq.centroids, pq._nested, cfg["bits"], codes, norms, q,
                               k=cfg["k"], candidates=cfg["candidates"],
                               coarse_precision=cfg["coarse_precision"])
+        elif cfg["mode"] == "ivf":
+            if nq_done == 0:
+                H = O.lsh_hyperplanes(cfg["n_bits"], cfg["d"], 0)
+                cells = O.ivf_cell_ids(codes, cfg["bits"], cfg["n_bits"], "lsh", H)
+                srt, off = O.ivf_csr(cells, 1 << cfg["n_bits"])
+            O.ivf_search_twostage(pq.R, pq.centroids, pq._nested, cfg["bits"], codes, norms,
+                                  srt, off, cfg["n_bits"], "lsh", H, q, k=cfg["k"],
+                                  candidates=cfg["candidates"], nprobe=cfg["nprobe"],
+                                  coarse_precision=cfg["coarse_precision"])
         elif cfg["mode"] == "batch":
             # search_batch over a block of 64 queries at a time (remex/core.py:721-778)
             O.search_batch(pq.R, pq.centroids, pq._nested, cfg["bits"], codes, norms,
@@ -298,7 +311,23 @@ def main():
         return out
     ss.local_topk = timed_local_topk
 
+    ivf = None
+    if cfg["mode"] == "ivf":
+        from polarquant_b200 import IVFCoarseIndex
+        if world > 1:
+            raise SystemExit("the ivf workload runs on one GPU")
+        ivf = IVFCoarseIndex(pq, cv, n_bits=cfg["n_bits"], mode="lsh", seed=0)
+
     def step(Qin):
+        if ivf is not None:
+            a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a_.record()
+            out = ivf.search_twostage_many(Qin, k=cfg["k"], candidates=cfg["candidates"],
+                                           nprobe=cfg["nprobe"],
+                                           coarse_precision=cfg["coarse_precision"])
+            b_.record()
+            kern_ms.append((a_, b_))
+            return out
         if cfg["mode"] == "twostage":
             return ss.search_twostage_many(Qin, k=cfg["k"], candidates=cfg["candidates"],
                                            coarse_precision=cfg["coarse_precision"])
@@ -307,7 +336,7 @@ def main():
     qrot0 = pq._rotate(Q, dev)
     p_scan = cfg["coarse_precision"] or cfg["bits"]
     k_scan = min(cfg["candidates"] or cfg["k"], rows.n)
-    batched = cfg["nq"] >= 64 and k_scan <= 256
+    batched = cfg["nq"] >= 64 and k_scan <= 256 and cfg["mode"] != "ivf"
 
     def barrier():
         if world > 1:
@@ -358,9 +387,14 @@ def main():
     ee0.record()
     for _ in range(args.steps):
         Qd = Qh.to(dev, non_blocking=True)
-        s, i = step(Qd)
-        ids, sc = i.cpu(), s.cpu()
-        d2h = ids.numel() * 8 + sc.numel() * 4
+        res = step(Qd)
+        if ivf is not None:
+            ids, sc = res
+            d2h = ids.size * 8 + sc.size * 4
+        else:
+            s, i = res
+            ids, sc = i.cpu(), s.cpu()
+            d2h = ids.numel() * 8 + sc.numel() * 4
     ee1.record()
     barrier()
     e2e_ms = ee0.elapsed_time(ee1) / args.steps
@@ -403,7 +437,22 @@ def main():
                  "frac": sgbs / hbm, "queries_per_launch": nsq, "launch_ms": sms,
                  "kernel": "scan_topk_kernel (+ merge), one corpus pass per query",
                  "peak_kind": peak_kind, "alg_bytes_per_launch": sbytes}
-    if not batched:
+    if ivf is not None:
+        # IVF: the gather-scan visits the probed cells' rows (row_bytes + 4 +
+        # 8-byte CSR id each); algorithmic bytes per launch from the index.
+        sizes = np.diff(ivf.cell_offsets)
+        Qh_ = Q.cpu().numpy()
+        visited = 0
+        for qi in range(cfg["nq"]):
+            visited += int(sizes[ivf.probe_cells(ivf.query_cell(Qh_[qi]),
+                                                 cfg["nprobe"])].sum())
+        ibytes = visited * (row_bytes + 8)
+        roof = {"bound": "hbm", "achieved": ibytes / (kms / 1e3) / 1e9, "peak": hbm,
+                "unit": "GB/s", "frac": ibytes / (kms / 1e3) / 1e9 / hbm, "traffic": None,
+                "kernel": "ivf_scan_kernel + rerank (whole pq_ivf_search call)",
+                "peak_kind": peak_kind, "alg_bytes_per_launch": ibytes, "launch_ms": kms,
+                "rows_visited_per_query": visited / cfg["nq"]}
+    elif not batched:
         roof = dict(scan_roof, traffic=None)
         kms = sms
     alg_bytes = cfg["nq"] * rows.n * row_bytes

@@ -190,6 +190,33 @@ int pq_rerank(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n,
               void* stream);
 
 /* ---------------------------------------------------------------------------
+ * IVF coarse index (remex/ivf.py).  mode 0 = 'lsh', 1 = 'rotated_prefix'.
+ * pq_ivf_cell_ids: cell id (uint16) of every row from the MSBs of its codes
+ *   (remex/ivf.py:162-214); lsh projections onto hyperplanes (n_bits x d f32)
+ *   are summed exactly in f64.
+ * pq_ivf_probe: per query the nprobe cells closest in Hamming distance to the
+ *   query cell, ties by cell id (remex/ivf.py:230-265); probe is nq x nprobe.
+ * pq_ivf_search: IVFCoarseIndex.search_coarse (rerank = 0: top-k of the coarse
+ *   ADC scores over the probed cells' rows, remex/ivf.py:301-374) or
+ *   .search_twostage (rerank = 1: top-`candidates` coarse rows, full-precision
+ *   rescoring, top-k, remex/ivf.py:376-436).  sorted_idx/offsets: the CSR
+ *   layout (rows grouped by cell, offsets n_cells + 1).  Each probed cell's
+ *   rows are split over `splits` blocks.  Slots past a query's candidate count
+ *   hold id -1.  Workspace: pq_ivf_workspace_bytes(nq, nprobe, splits, C).
+ * ------------------------------------------------------------------------- */
+int pq_ivf_cell_ids(const uint8_t* packed, int64_t ldb, int64_t n, int d, int bits, int n_bits,
+                    int mode, const float* hyperplanes, uint16_t* cells, void* stream);
+int pq_ivf_probe(const float* qrot, int nq, int d, int n_bits, int mode, const float* hyperplanes,
+                 int nprobe, int* probe, int* query_cells, void* stream);
+size_t pq_ivf_workspace_bytes(int nq, int nprobe, int splits, int candidates);
+int pq_ivf_search(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
+                  int bits, int coarse_precision, const float* qrot, int nq,
+                  const float* cent_coarse, const float* cent_full, int n_bits, int mode,
+                  const float* hyperplanes, const int64_t* sorted_idx, const int64_t* offsets,
+                  int nprobe, int splits, int candidates, int k, int rerank, float* out_scores,
+                  int64_t* out_ids, void* ws, size_t ws_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Merge of per-part top-k lists: in_s/in_ids are parts x nq x kin (as written
  * by the per-rank scans, ids already global); out is nq x k, k <= kin*parts,
  * k <= PQ_TOPK_MAX.  Used after the NCCL all-gather of the row-sharded search.

@@ -9,6 +9,7 @@ library (include/polarquant_b200.h).
 import warnings
 
 from .core import CompressedVectors, PackedVectors, Quantizer
+from .ivf import IVFCoarseIndex
 from .packing import pack, packed_nbytes, unpack
 from .params import lloyd_max_codebook, nested_codebooks
 
@@ -16,6 +17,7 @@ __version__ = "0.5.0"
 __all__ = [
     "Quantizer", "CompressedVectors", "PackedVectors",
     "PolarQuantizer",
+    "IVFCoarseIndex",
     "lloyd_max_codebook", "nested_codebooks",
     "pack", "unpack", "packed_nbytes",
 ]

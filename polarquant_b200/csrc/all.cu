@@ -6,4 +6,5 @@
 #include "sort.cu"
 #include "encode.cu"
 #include "batched.cu"
+#include "ivf.cu"
 #include "noalloc.cu"

@@ -102,9 +102,11 @@ class ShardedSearch:
     def all_gather(self, t: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
             return t.unsqueeze(0)
-        out = torch.empty((self.world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
-        dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
-        return out
+        t = t.contiguous()
+        out = torch.empty((self.world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype,
+                          device=t.device)
+        dist.all_gather_into_tensor(out, t, group=self.group)
+        return out.view((self.world,) + tuple(t.shape))
 
     def _gathered_topk(self, s: torch.Tensor, i: torch.Tensor, k: int, k_out: int):
         s, i = pad_topk(s, i, k)
