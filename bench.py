@@ -1,18 +1,29 @@
 """Benchmark of the B200 encode + ADC-search path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c2|c1]
+                    [--workload c4|c3|c2|c5|c1|c4s] [--quick]
 
 One JSON line on rank 0.  Workloads (synthetic, seeded, generated on the GPU):
 
-  c2 (default): d=768, bits=8, 1,000,000 corpus vectors = 1,000 unit centres
+  c4 (default): d=1536, bits=4, 100,000,000 corpus vectors = 10,000 unit
+      centres + N(0, (0.2/sqrt(d))^2) noise, re-normalised, row-sharded across
+      the ranks; 10,000 queries drawn the same way; batched ADC with k=100 and
+      an NCCL all-gather merge.  A step = the whole 10,000-query batch.
+  c2: d=768, bits=8, 1,000,000 corpus vectors = 1,000 unit centres
       + N(0, (0.3/sqrt(d))^2) noise, re-normalised; 1,000 queries drawn the
       same way with another seed; search_twostage(coarse_precision=4,
       candidates=200, k=10).  A step = the whole 1,000-query batch.  Metric:
       queries/s (whole job).  The corpus (768 MB) is larger than L2, so no
       flush is needed between steps.
+  c3: encode sweep, d=1024, 4,000,000 N(0, I) rows scaled by norms drawn
+      log-uniform in [0.5, 2]; a step encodes all rows at bits = 2, 3, 4 and 8.
+      Metric: vectors/s (16M encodes per step).
+  c5: IVF (lsh, 12 bits = 4096 cells), d=384, bits=4, 10,000,000 rows from
+      4,096 centres (noise 0.1/sqrt(d)), nprobe=32, 2-bit coarse, 500
+      candidates, 4-bit rerank, k=10, 1,000 queries (one GPU).
   c1: d=384, bits=4, 10,000 N(0,1) unit vectors, 200 queries, search_adc k=10
       (L2-resident corpus).
+  c4s: the c4 kernel on a 4M-row slice (for ncu captures).
 
 Multi-GPU: rows are sharded contiguously across ranks (torch.distributed,
 NCCL); each step runs the exact two-round merge (all-gather of coarse
@@ -45,6 +56,9 @@ WORKLOADS = {
                candidates=200, coarse_precision=4, mode="twostage",
                name="twostage d=768 bits=8 n=1M clustered(1000, 0.3/sqrt(d)) q=1000 "
                     "C=200 cp=4 k=10"),
+    "c3": dict(d=1024, bits=4, n=4_000_000, nq=0, n_centres=0, sigma=0.0, k=0, lognorm=True,
+               candidates=0, coarse_precision=None, mode="encode", widths=(2, 3, 4, 8),
+               name="encode d=1024 n=4M N(0,I) x lognormal-norm[0.5,2], bits 2/3/4/8"),
     "c1": dict(d=384, bits=4, n=10_000, nq=200, n_centres=0, sigma=0.0, k=10,
                candidates=0, coarse_precision=None, mode="adc",
                name="search_adc d=384 bits=4 n=10k N(0,1) unit q=200 k=10"),
@@ -87,6 +101,9 @@ def gen_rows(torch, device, cfg, start, stop, seed, centres):
             lab = torch.randint(0, centres.shape[0], (b - a,), generator=g, device=device)
             x = centres[lab] + x * (cfg["sigma"] / np.sqrt(d))
         x = x / torch.linalg.vector_norm(x, dim=1, keepdim=True)
+        if cfg.get("lognorm"):
+            u = torch.rand((b - a, 1), generator=g, device=device)
+            x = x * torch.exp(np.log(0.5) + u * (np.log(2.0) - np.log(0.5)))
         lo, hi = max(a, start), min(b, stop)
         out[lo - start:hi - start] = x[lo - a:hi - a]
     return out
@@ -220,19 +237,154 @@ def cpu_baseline(cfg, X_sample, Q_host, pq, budget_s=20.0):
             "encode_vectors_per_s": m / t_enc}
 
 
+def encode_bench(args, cfg, torch, dist, dev, world, rank):
+    """c3: every step encodes this rank's rows at each width (remex/core.py:484-511)."""
+    from polarquant_b200 import Quantizer, _lib
+    from polarquant_b200.distributed import shard_bounds
+    from polarquant_b200.encode import alloc_corpus, encode_into
+    widths = cfg["widths"]
+    qz = {b: Quantizer(cfg["d"], bits=b, seed=42) for b in widths}
+    sample_rows = 100_000
+    if args.impl == "reference":
+        Xs = gen_rows(torch, dev, cfg, 0, sample_rows, seed=3, centres=None).cpu().numpy()
+        from oracle import remex_oracle as O
+        t0 = time.perf_counter()
+        for b in widths:
+            O.encode(Xs, qz[b].R, qz[b].boundaries)
+        dt = time.perf_counter() - t0
+        v = sample_rows * len(widths) / dt
+        line = {"metric": "encode vectors/s", "value": v, "unit": "vectors/s",
+                "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": cfg["name"]},
+                "cpu_baseline": {"value": v, "unit": "vectors/s", "cores": os.cpu_count(),
+                                 "kind": "port",
+                                 "sample": f"NumPy encode of {sample_rows} rows at each of bits "
+                                           f"{list(widths)} in {dt:.1f} s"},
+                "e2e": {"value": v, "unit": "vectors/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    r0, r1 = shard_bounds(cfg["n"], world, rank)
+    X = gen_rows(torch, dev, cfg, r0, r1, seed=3, centres=None)
+    corp = {b: alloc_corpus(qz[b], r1 - r0, dev) for b in widths}
+
+    def step():
+        for b in widths:
+            encode_into(qz[b], X, corp[b], 0)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+    launches0 = _lib.query("pq_launch_count")
+    clk = ClockSampler(dev.index)
+    clk.start()
+    barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    per = {b: [] for b in widths}
+    t0.record()
+    for _ in range(args.steps):
+        for b in widths:
+            a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a_.record()
+            encode_into(qz[b], X, corp[b], 0)
+            b_.record()
+            per[b].append((a_, b_))
+    t1.record()
+    barrier()
+    clocks = clk.stop()
+    launches = _lib.query("pq_launch_count") - launches0
+    ms = t0.elapsed_time(t1) / args.steps
+    ms_t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    nrows = cfg["n"] * len(widths)
+    per_w = {str(b): (r1 - r0) * world / (np.mean([x.elapsed_time(y) for x, y in per[b]]) / 1e3)
+             for b in widths}
+    hbm, bf16, peak_kind = measured_peaks()
+    flops = 2.0 * (r1 - r0) * cfg["d"] ** 2 * len(widths)
+    ach = flops / (ms / 1e3) / 1e12
+    line = {"metric": "encode vectors/s", "value": nrows / (ms / 1e3), "unit": "vectors/s",
+            "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32 in, fp16 hi/lo split on tcgen05, codes out",
+            "data": "synthetic",
+            "config": {"workload": cfg["name"], "global_batch": cfg["n"],
+                       "parallelism": f"row-shard x{world}",
+                       "l2": "16.8 GB input, larger than L2"},
+            "per_width_vectors_per_s": per_w,
+            "roofline": {"bound": "tensor", "achieved": ach, "peak": bf16, "unit": "TFLOP/s",
+                         "frac": ach / bf16, "traffic": None,
+                         "kernel": "encode_prep_kernel + encode_gemm_kernel (whole encode; 3 "
+                                   "MMAs per algorithmic MAC)",
+                         "peak_kind": f"{peak_kind} dense bf16 (burst)",
+                         "alg_flops_per_step": flops},
+            "gpu_launches": int(launches), "clocks": clocks}
+    if not args.quick:
+        # e2e: host f32 rows in, packed codes + norms back (one width per step).
+        sub = min(r1 - r0, 1_000_000)
+        Xh = torch.empty((sub, cfg["d"]), dtype=torch.float32, pin_memory=True)
+        Xh.copy_(X[:sub].cpu())
+        q4 = qz[4]
+        q4.encode(Xh[:1024])
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        cv = q4.encode(Xh.to(dev, non_blocking=True))
+        packed = cv._rows.buf[: sub * cv._rows.ldb].cpu()
+        nrm = cv._rows.norms.cpu()
+        e1.record()
+        barrier()
+        ems = e0.elapsed_time(e1)
+        line["e2e"] = {"value": sub * world / (ems / 1e3), "unit": "vectors/s",
+                       "h2d_bytes_per_step": int(sub * cfg["d"] * 4),
+                       "d2h_bytes_per_step": int(packed.numel() + nrm.numel() * 4),
+                       "note": "public encode() on 1M host rows at bits=4, results copied back"}
+        if rank == 0 and world == 1:
+            Xs = X[:sample_rows].cpu().numpy()
+            from oracle import remex_oracle as O
+            t0_ = time.perf_counter()
+            for b in widths:
+                O.encode(Xs, qz[b].R, qz[b].boundaries)
+            dt = time.perf_counter() - t0_
+            line["cpu_baseline"] = {"value": sample_rows * len(widths) / dt,
+                                    "unit": "vectors/s", "cores": os.cpu_count(),
+                                    "kind": "port",
+                                    "sample": f"NumPy encode of {sample_rows} rows at each of "
+                                              f"bits {list(widths)} in {dt:.1f} s"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # ---------------------------------------------------------------------------
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="c4", choices=sorted(WORKLOADS))
+    ap.add_argument("--path", default="auto", choices=["auto", "scan", "batch"],
+                    help="force the streaming scan or the tensor-core batch path")
+    ap.add_argument("--queries", type=int, default=0, help="override the query count")
     ap.add_argument("--quick", action="store_true",
                     help="timed steps only (no e2e, scan roofline or CPU baseline); for profiling")
     args = ap.parse_args()
-    cfg = WORKLOADS[args.workload]
+    cfg = dict(WORKLOADS[args.workload])
+    if args.queries:
+        cfg["nq"] = args.queries
 
     import torch
     import torch.distributed as dist
@@ -257,6 +409,8 @@ def main():
     from polarquant_b200 import Quantizer, _lib
     from polarquant_b200.distributed import ShardedSearch, shard_bounds
 
+    if cfg["mode"] == "encode":
+        return encode_bench(args, cfg, torch, dist, dev, world, rank)
     pq = Quantizer(cfg["d"], bits=cfg["bits"], seed=42)
     centres = make_centres(torch, dev, cfg, seed=7)
     Q = make_queries(torch, dev, cfg, centres)
@@ -299,6 +453,8 @@ def main():
     enc_vps = (r1 - r0) / (enc_ms / 1e3)
     cv = CompressedVectors._from_device(rows)
     ss = ShardedSearch(pq, cv, r0, cfg["n"])
+    if args.path != "auto":
+        ss.force = args.path
     kern_ms = []
     _local_topk = ss.local_topk
 
@@ -336,7 +492,8 @@ def main():
     qrot0 = pq._rotate(Q, dev)
     p_scan = cfg["coarse_precision"] or cfg["bits"]
     k_scan = min(cfg["candidates"] or cfg["k"], rows.n)
-    batched = cfg["nq"] >= 64 and k_scan <= 256 and cfg["mode"] != "ivf"
+    batched = (cfg["nq"] >= 64 and k_scan <= 256 and cfg["mode"] != "ivf"
+               and args.path != "scan") or args.path == "batch"
 
     def barrier():
         if world > 1:
@@ -384,8 +541,9 @@ def main():
     barrier()
     ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     d2h = 0
+    e2e_steps = max(1, min(args.steps, int(np.ceil(10_000.0 / max(ms, 1.0)))))
     ee0.record()
-    for _ in range(args.steps):
+    for _ in range(e2e_steps):
         Qd = Qh.to(dev, non_blocking=True)
         res = step(Qd)
         if ivf is not None:
@@ -397,7 +555,7 @@ def main():
             d2h = ids.numel() * 8 + sc.numel() * 4
     ee1.record()
     barrier()
-    e2e_ms = ee0.elapsed_time(ee1) / args.steps
+    e2e_ms = ee0.elapsed_time(ee1) / e2e_steps
     e2e_t = torch.tensor([e2e_ms], device=dev)
     if world > 1:
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)

@@ -60,6 +60,7 @@ class ShardedSearch:
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.force = None  # "scan" / "batch" pins the per-rank ADC path
 
     # -- per-rank compute (CUDA library); tests may override ---------------------
     @property
@@ -72,7 +73,7 @@ class ShardedSearch:
 
     def local_topk(self, qrot: torch.Tensor, k: int, precision: int):
         rows = self.shard._device()
-        s, i = self.q._scan(rows, qrot, k, precision)
+        s, i = self.q._scan(rows, qrot, k, precision, force=self.force)
         return s, i + self.row_offset
 
     def local_rerank(self, qrot: torch.Tensor, cand: torch.Tensor, k: int):
