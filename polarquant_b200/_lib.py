@@ -37,6 +37,7 @@ SIGNATURES = {
     "pq_decode_workspace_bytes": (_Z, [_L, _I]),
     "pq_decode": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _P, _P, _P, _Z, _P]),
     "pq_adc_scan_workspace_bytes": (_Z, [_L, _I, _I, _I]),
+    "pq_adc_scan_kernel": (_I, [_L, _I, _I, _I, _I, _I, _L]),
     "pq_adc_batch_workspace_bytes": (_Z, [_L, _I, _I, _I]),
     "pq_adc_scan_noalloc_scratch_bytes": (_Z, []),
     "pq_adc_scan_noalloc": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _I, _P, _I, _L, _P, _P, _P]),

@@ -5,6 +5,8 @@
 #include "rotate.cu"
 #include "sort.cu"
 #include "encode.cu"
+#include "scan2.cu"
 #include "batched.cu"
+#include "batched2.cu"
 #include "ivf.cu"
 #include "noalloc.cu"

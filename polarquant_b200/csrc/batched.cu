@@ -679,9 +679,9 @@ static size_t bat_ws_carve(const BatPlan& b, int nq, int K, void* ws, size_t ws_
 
 using namespace pqb;
 
-// Runs the batched kernel; leaves per-(query, row chunk) top-K lists in ws
-// (layout [nq][rchunks][K]) and returns their location.
-static int run_batched(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
+// Runs the one-CTA batched kernel; leaves per-(query, row chunk) top-K lists
+// in ws (layout [nq][rchunks][K]) and returns their location.
+static int run_batched_1cta(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
                        int bits, int precision, const float* qrot, int nq, const float* cent, int K,
                        int64_t row_offset, void* ws, size_t ws_bytes, cudaStream_t st,
                        float** parts_s, long long** parts_id, int* nparts) {
@@ -737,7 +737,7 @@ static int run_batched(const uint8_t* packed, int64_t ldb, const float* norms, i
   return PQ_OK;
 }
 
-static size_t batched_ws(int64_t n, int d, int nq, int k) {
+static size_t batched_ws_1cta(int64_t n, int d, int nq, int k) {
   if (n <= 0 || nq <= 0 || k <= 0 || d <= 0) return 256;
   const BatPlan b = bat_plan(n, d, nq, k);
   BatWs w;

@@ -276,14 +276,25 @@ static int launch_merge(const float* in_s, const long long* in_id, int parts, in
   return PQ_OK;
 }
 
-// Scan every query against all rows, leaving per-block candidates in ws.
+static int try_scan2(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
+                     int bits, int precision, const float* qrot, int nq, const float* cent,
+                     int K, float* cand_s, long long* cand_id, cudaStream_t st, int* nblk,
+                     bool* used);
+
+// Scan every query against all rows, leaving per-block candidates in ws:
+// list b of query q at (q * nblk + b) * K, *nblk_out <= scan_blocks(n, nq).
+// 4- and 8-bit corpora run the TMA-staged scan (scan2.cu) when it fits.
 static int run_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
                     int bits, int precision, const float* qrot, int nq, const float* cent, int K,
-                    float* cand_s, long long* cand_id, cudaStream_t st) {
+                    float* cand_s, long long* cand_id, cudaStream_t st, int* nblk_out) {
+  bool used = false;
+  int rc = try_scan2(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent, K, cand_s,
+                     cand_id, st, nblk_out, &used);
+  if (rc || used) return rc;
   const int64_t per = scan_rows_per_block(n, nq);
   const int nblk = scan_blocks(n, nq);
+  *nblk_out = nblk;
   const size_t sm = scan_smem(d, precision, K);
-  int rc = PQ_OK;
   dim3 grid(nblk, nq);
   PQ_DISPATCH_BP(bits, precision, {
     auto kern = scan_topk_kernel<B_, P_>;
@@ -341,12 +352,12 @@ int pq_adc_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
   if (k > PQ_TOPK_MAX)
     return adc_large_k(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent, k, row_offset,
                        out_scores, out_ids, ws, st);
-  const int nblk = scan_blocks(n, nq);
+  int nblk = scan_blocks(n, nq);
   Carve cv(ws, ws_bytes);
   const size_t c = (size_t)nq * nblk * k;
   float* cs = cv.take<float>(c);
   long long* ci = cv.take<long long>(c);
-  rc = run_scan(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent, k, cs, ci, st);
+  rc = run_scan(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent, k, cs, ci, st, &nblk);
   if (rc) return rc;
   return launch_merge(cs, ci, nblk, k, (long long)nblk * k, k, nq, k, row_offset, out_scores,
                       (long long*)out_ids, st);
@@ -403,7 +414,7 @@ int pq_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
     cs = cv.take<float>(c);
     ci = cv.take<long long>(c);
     rc = run_scan(packed, ldb, norms, n, d, bits, coarse_precision, qrot, nq, cent_coarse,
-                  candidates, cs, ci, st);
+                  candidates, cs, ci, st, &nblk);
   }
   if (rc) return rc;
   const size_t sm = rerank_smem(d, bits, candidates, k);

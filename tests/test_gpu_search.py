@@ -302,3 +302,16 @@ def test_twostage_batched_coarse(gpu, bits, cands, cp):
                                    candidates=cands, coarse_precision=cp)
         bad += not O.topk_equal_up_to_ties(GI[q], GS[q], ri, rs, rtol=RTOL)
     assert bad == 0
+
+
+@pytest.mark.parametrize("bits", [1, 3, 4, 8])
+def test_batched_adc_full_query_tiles(gpu, bits):
+    """Query batches spanning several 256-query tiles (both CTAs of each pair
+    busy) over many row chunks, against the oracle's search_batch."""
+    pq, cv, idx, norms, qs = make_case(bits, d=256, n=40000, nq=520, data_seed=bits)
+    RI, RS = O.search_batch(pq.R, pq.centroids, pq._nested, bits, idx, norms, qs, k=64,
+                            precision=max(1, bits - 1))
+    GI, GS = _batched(pq, cv, qs, 64, max(1, bits - 1), "batch")
+    bad = sum(not O.topk_equal_up_to_ties(GI[q], GS[q], RI[q], RS[q], rtol=RTOL)
+              for q in range(len(qs)))
+    assert bad == 0
