@@ -533,7 +533,7 @@ batched_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_const
           __syncwarp();
           tc::tmem_ld16(taddr + (uint32_t)c0, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
           tc::tmem_ld16(taddr + (uint32_t)c0 + 16u, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
-          tc::tmem_ld_wait();
+          tc::tmem_ld_wait(v);
           uint32_t need = __ballot_sync(0xffffffffu, qv && cnt + 32 > p.cap);
           while (need) {
             const int src = __ffs(need) - 1;

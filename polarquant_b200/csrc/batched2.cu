@@ -24,7 +24,8 @@ constexpr int kPM = 128;       // queries per CTA (256 per pair)
 constexpr int kPN = 256;       // rows per pair tile
 constexpr int kPNh = 128;      // rows per CTA
 constexpr int kPStages = 3;
-constexpr int kPThreads = 14 * 32;
+constexpr int kPThreads = 15 * 32;
+constexpr int kPRawBytes = 16384;  // ring of raw code tiles (TMA), per CTA
 
 // Decoder geometry for B-bit codes: one K block (64 codes) of a row is RB
 // bytes, read as PER_ROW segments of SEG bytes (the one-CTA kernel's
@@ -39,6 +40,8 @@ struct PairDec {
   static constexpr int RB = DecSeg<B>::RB;
   static constexpr int UPT = kPNh * PER_ROW / (DW * 32);
   static_assert(UPT >= 1 && UPT * DW * 32 == kPNh * PER_ROW, "decoder split");
+  static constexpr int RAWSTAGE = kPNh * RB;   // one K block of this CTA's 128 rows
+  static constexpr int RAW = kPRawBytes / RAWSTAGE;
 };
 
 struct PairWalk {
@@ -65,28 +68,9 @@ __device__ __forceinline__ void pair_next(PairWalk& w, const BatArgs& p, int nta
 }
 
 template <int B>
-__device__ __forceinline__ void pair_load(const BatArgs& p, const PairWalk& w, int dt, int half,
-                                          uint32_t (&seg)[PairDec<B>::UPT][PairDec<B>::WORDS]) {
-  using S = PairDec<B>;
-  const int64_t tr0 = w.r0 + (int64_t)w.tile * kPN + half;
-#pragma unroll
-  for (int i = 0; i < S::UPT; ++i) {
-    const int u = dt + i * S::DW * 32;
-    const int r = u / S::PER_ROW, sg = u % S::PER_ROW;
-    const int64_t row = tr0 + r;
-    if (row < w.r1) {
-      load_seg<B>(p.packed + row * p.ldb + (int64_t)w.kb * S::RB + sg * S::SEG, seg[i]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < S::WORDS; ++j) seg[i][j] = 0u;
-    }
-  }
-}
-
-template <int B>
 __global__ void __launch_bounds__(kPThreads, 1)
 pair_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant__ CUtensorMap tmQlo,
-                const BatArgs p) {
+                const __grid_constant__ CUtensorMap tmRaw, const BatArgs p) {
   using S = PairDec<B>;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t raw = tc::smem_u32(smem_raw);
@@ -98,14 +82,20 @@ pair_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant
   const uint32_t meta = base + kPStages * STAGE;
   uint8_t* gmeta = gbase + kPStages * STAGE;
   auto bar = [&](int i) { return meta + 8u * (uint32_t)i; };
-  constexpr int FULLA = 0, FULLB = kPStages, PEERA = 2 * kPStages, EMPTY = 3 * kPStages,
+  constexpr int FULLA = 0, FULLB = kPStages, PEER = 2 * kPStages, EMPTY = 3 * kPStages,
                 TFULL = 4 * kPStages, TEMPTY = 4 * kPStages + 2, DRAIN = 4 * kPStages + 4,
-                NBAR = 4 * kPStages + 5;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(gmeta + 8 * NBAR);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(gmeta + 8 * NBAR + 4);
-  uint32_t* slut = reinterpret_cast<uint32_t*>(gmeta + 8 * NBAR + 16);       // 256 entries
-  float* scratch_s = reinterpret_cast<float*>(gmeta + 8 * NBAR + 16 + 1024);  // 4 x 512
-  int* scratch_i = reinterpret_cast<int*>(gmeta + 8 * NBAR + 16 + 1024 + 4 * kBatScratch * 4);
+                RAWFULL = 4 * kPStages + 5, RAWEMPTY = RAWFULL + S::RAW,
+                NBAR = RAWEMPTY + S::RAW;
+  constexpr int NBAR_MAX = 4 * kPStages + 5 + 2 * 8;  // layout is the same for every B
+  static_assert(NBAR <= NBAR_MAX, "barrier area");
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(gmeta + 8 * NBAR_MAX);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gmeta + 8 * NBAR_MAX + 4);
+  uint32_t* slut = reinterpret_cast<uint32_t*>(gmeta + 8 * NBAR_MAX + 16);       // 256 entries
+  float* scratch_s = reinterpret_cast<float*>(gmeta + 8 * NBAR_MAX + 16 + 1024);  // 4 x 512
+  int* scratch_i = reinterpret_cast<int*>(gmeta + 8 * NBAR_MAX + 16 + 1024 + 4 * kBatScratch * 4);
+  const uint32_t raw_ring =
+      (meta + 8 * NBAR_MAX + 16 + 1024 + 4 * kBatScratch * 8 + 127u) & ~127u;
+  const uint8_t* graw = smem_raw + (raw_ring - raw);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = tc::cluster_ctarank();
@@ -114,8 +104,8 @@ pair_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPStages; ++s) {
       tc::mbar_init(bar(FULLA + s), 1);
-      tc::mbar_init(bar(FULLB + s), 2 * S::DW);
-      tc::mbar_init(bar(PEERA + s), 1);
+      tc::mbar_init(bar(FULLB + s), S::DW);
+      tc::mbar_init(bar(PEER + s), 1);
       tc::mbar_init(bar(EMPTY + s), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -123,10 +113,15 @@ pair_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant
       tc::mbar_init(bar(TEMPTY + b), 8);
     }
     tc::mbar_init(bar(DRAIN), 1);
+    for (int r = 0; r < S::RAW; ++r) {
+      tc::mbar_init(bar(RAWFULL + r), 1);
+      tc::mbar_init(bar(RAWEMPTY + r), S::DW);
+    }
     *abort_flag = 0;
     tc::fence_barrier_init();
     tc::prefetch_tmap(&tmQhi);
     tc::prefetch_tmap(&tmQlo);
+    tc::prefetch_tmap(&tmRaw);
   }
   for (int i = threadIdx.x; i < p.lut_size; i += blockDim.x) slut[i] = p.lut[i];
   if (warp == 1) tc::tmem_alloc_pair(tc::smem_u32(tmem_holder), 512u);
@@ -174,7 +169,7 @@ pair_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant
     }
   } else if (warp == 1) {
     if (lane == 0 && !leader) {
-      // ---------------- relay (odd CTA): query tile landed ----------------
+      // ---------------- relay (odd CTA): stage s of this CTA is complete ----------------
       int it = 0;
       bool ok = true;
       for (int t = pair; t < ntasks && ok; t += npairs) {
@@ -186,11 +181,12 @@ pair_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant
           for (int kb = 0; kb < p.nk; ++kb, ++it) {
             const int s = it % kPStages;
             const uint32_t ph = (uint32_t)(it / kPStages) & 1u;
-            if (!tc::mbar_wait(bar(FULLA + s), ph, abort_flag, tc::kErrWaitTmaFull)) {
+            if (!tc::mbar_wait(bar(FULLA + s), ph, abort_flag, tc::kErrWaitTmaFull) ||
+                !tc::mbar_wait(bar(FULLB + s), ph, abort_flag, tc::kErrWaitTmaFull)) {
               ok = false;
               break;
             }
-            tc::mbar_arrive_cluster(lead_bar(PEERA + s));
+            tc::mbar_arrive_cluster(lead_bar(PEER + s));
           }
         }
       }
@@ -218,8 +214,8 @@ pair_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant
             const int s = it % kPStages;
             const uint32_t ph = (uint32_t)(it / kPStages) & 1u;
             if (!tc::mbar_wait(bar(FULLA + s), ph, abort_flag, tc::kErrWaitTmaFull) ||
-                !tc::mbar_wait_cluster(bar(PEERA + s), ph, abort_flag, tc::kErrWaitTmaFull) ||
-                !tc::mbar_wait_cluster(bar(FULLB + s), ph, abort_flag, tc::kErrWaitTmaFull)) {
+                !tc::mbar_wait(bar(FULLB + s), ph, abort_flag, tc::kErrWaitTmaFull) ||
+                !tc::mbar_wait_cluster(bar(PEER + s), ph, abort_flag, tc::kErrWaitTmaFull)) {
               ok = false;
               break;
             }
@@ -246,9 +242,44 @@ pair_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant
       volatile int never = 0;
       tc::mbar_wait(bar(DRAIN), 0, &never, tc::kErrWaitAccFull);
     }
+  } else if (warp == 14) {
+    if (lane == 0) {
+      // ---------------- TMA producer: raw code tiles of this CTA's 128 rows ----------------
+      const int half = (int)rank * kPNh;
+      int it = 0;
+      bool ok = true;
+      for (int t = pair; t < ntasks && ok; t += npairs) {
+        const int rc = t / p.qtiles;
+        const int64_t r0 = (int64_t)rc * p.rows_per_chunk;
+        const int64_t r1 = min(p.n, r0 + p.rows_per_chunk);
+        const int tiles = (int)((r1 - r0 + kPN - 1) / kPN);
+        for (int tile = 0; tile < tiles && ok; ++tile) {
+          const int y = (int)(r0 + (int64_t)tile * kPN + half);
+          for (int kb = 0; kb < p.nk; ++kb, ++it) {
+            const int r = it % S::RAW;
+            const uint32_t ph = (uint32_t)(it / S::RAW) & 1u;
+            if (!tc::mbar_wait(bar(RAWEMPTY + r), ph ^ 1u, abort_flag, tc::kErrWaitStageEmpty)) {
+              ok = false;
+              break;
+            }
+            tc::mbar_arrive_expect_tx(bar(RAWFULL + r), (uint32_t)S::RAWSTAGE);
+            tc::tma_load_2d(raw_ring + (uint32_t)(r * S::RAWSTAGE), &tmRaw, kb * S::RB, y,
+                            bar(RAWFULL + r));
+          }
+        }
+      }
+      for (int j = it - S::RAW; j < it; ++j) {
+        if (j < 0) continue;
+        volatile int never = 0;
+        tc::mbar_wait(bar(RAWFULL + j % S::RAW), (uint32_t)(j / S::RAW) & 1u, &never,
+                      tc::kErrWaitTmaFull);
+      }
+    }
   } else if (warp >= 6) {
     if (warp < 6 + S::DW) {
       // ---------------- decoder: this CTA's 128 rows of each tile ----------------
+      // Raw codes arrive by TMA in a ring several K blocks ahead; each thread
+      // decodes UPT segments (rows r, byte segments sg) of the current block.
       const int dt = threadIdx.x - 6 * 32;
       const int half = (int)rank * kPNh;
       PairWalk w;
@@ -256,15 +287,30 @@ pair_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant
       w.tile = 0;
       w.kb = 0;
       if (w.t < ntasks) pair_task(w, p);
-      uint32_t cur[S::UPT][S::WORDS], nxt[S::UPT][S::WORDS];
-      if (w.t < ntasks) pair_load<B>(p, w, dt, half, cur);
       for (int it = 0; w.t < ntasks; ++it) {
+        const int rr = it % S::RAW;
+        const uint32_t rph = (uint32_t)(it / S::RAW) & 1u;
         const PairWalk here = w;
         pair_next(w, p, ntasks, npairs);
-        if (w.t < ntasks) pair_load<B>(p, w, dt, half, nxt);
         const int s = it % kPStages;
         const uint32_t ph = (uint32_t)(it / kPStages) & 1u;
-        if (!tc::mbar_wait(bar(EMPTY + s), ph ^ 1u, abort_flag, tc::kErrWaitStageEmpty)) break;
+        if (!tc::mbar_wait(bar(RAWFULL + rr), rph, abort_flag, tc::kErrWaitTmaFull) ||
+            !tc::mbar_wait(bar(EMPTY + s), ph ^ 1u, abort_flag, tc::kErrWaitStageEmpty))
+          break;
+        uint32_t cur[S::UPT][S::WORDS];
+        const uint8_t* rawp = graw + rr * S::RAWSTAGE;
+#pragma unroll
+        for (int i = 0; i < S::UPT; ++i) {
+          const int u = dt + i * S::DW * 32;  // = r * PER_ROW + sg: byte offset u * SEG
+          if constexpr (S::SEG == 16) {
+            const uint4 v = *reinterpret_cast<const uint4*>(rawp + u * 16);
+            cur[i][0] = v.x; cur[i][1] = v.y; cur[i][2] = v.z; cur[i][3] = v.w;
+          } else {
+#pragma unroll
+            for (int j = 0; j < S::WORDS; ++j)
+              cur[i][j] = *reinterpret_cast<const uint32_t*>(rawp + u * S::SEG + 4 * j);
+          }
+        }
         uint8_t* xh = gbase + (size_t)s * STAGE + 2 * QPLANE;
         uint8_t* xl = xh + XPLANE;
         const int64_t tr0 = here.r0 + (int64_t)here.tile * kPN + half;
@@ -296,18 +342,14 @@ pair_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant
             *reinterpret_cast<uint4*>(xl + off) = vl;
           }
         }
-        // Generic-proxy stores become visible to the tensor core (async proxy)
-        // before the even CTA's MMA issuer learns of them.
+        // Generic-proxy stores become visible to the tensor core (async proxy);
+        // the odd CTA's relay forwards completion to the even CTA.
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) {
-          if (leader) tc::mbar_arrive(bar(FULLB + s));
-          else tc::mbar_arrive_cluster(lead_bar(FULLB + s));
+          tc::mbar_arrive(bar(FULLB + s));
+          tc::mbar_arrive(bar(RAWEMPTY + rr));  // the raw codes were consumed by the stores
         }
-#pragma unroll
-        for (int i = 0; i < S::UPT; ++i)
-#pragma unroll
-          for (int j = 0; j < S::WORDS; ++j) cur[i][j] = nxt[i][j];
       }
     }
   } else {
@@ -349,7 +391,7 @@ pair_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant
           __syncwarp();
           tc::tmem_ld16(taddr + (uint32_t)c0, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
           tc::tmem_ld16(taddr + (uint32_t)c0 + 16u, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
-          tc::tmem_ld_wait();
+          tc::tmem_ld_wait(v);
           uint32_t need = __ballot_sync(0xffffffffu, qv && cnt + 32 > p.cap);
           while (need) {
             const int src = __ffs(need) - 1;
@@ -359,17 +401,18 @@ pair_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant
             warp_select(src, lane, cnt, sbs, sbi, p.K, cnt, thr);
           }
           const int64_t rb = tr0 + c0;
-          if (qv && rb < r1) {
+          // The 32 rows' norms: one coalesced load, broadcast by shuffles.
+          const float my_norm = (rb + lane < r1) ? __ldg(p.norms + rb + lane) : 0.f;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int64_t row = rb + i;
-              if (row < r1) {
-                const float sc = __uint_as_float(v[i]) * qs * __ldg(p.norms + row);
-                if (sc > thr) {
-                  bs[cnt] = sc;
-                  bi[cnt] = (int)row;
-                  ++cnt;
-                }
+          for (int i = 0; i < 32; ++i) {
+            const float nr = __shfl_sync(0xffffffffu, my_norm, i);
+            const int64_t row = rb + i;
+            if (qv && row < r1) {
+              const float sc = __uint_as_float(v[i]) * qs * nr;
+              if (sc > thr) {
+                bs[cnt] = sc;
+                bi[cnt] = (int)row;
+                ++cnt;
               }
             }
           }
@@ -411,8 +454,15 @@ struct PairPlan {
 };
 
 static size_t pair_smem() {
-  return 1024 + (size_t)kPStages * (2 * kPM * 128 + 2 * kPNh * 128) + 8 * (4 * kPStages + 5) +
-         16 + 1024 + (size_t)4 * kBatScratch * 8 + 256;
+  return 1024 + (size_t)kPStages * (2 * kPM * 128 + 2 * kPNh * 128) + 8 * (4 * kPStages + 5 + 16) +
+         16 + 1024 + (size_t)4 * kBatScratch * 8 + 128 + kPRawBytes;
+}
+
+// The pair kernel covers 2-, 4- and 8-bit codes (raw K blocks of 16, 32 and
+// 64 bytes per row, a whole number of 16-byte TMA units) and corpora of at
+// least one pair tile.
+static bool pair_covers(int64_t n, int bits) {
+  return (bits == 2 || bits == 4 || bits == 8) && n >= kPN;
 }
 
 static void pair_config(cudaLaunchConfig_t* cfg, cudaLaunchAttribute* at, int grid,
@@ -513,7 +563,7 @@ static int run_batched(const uint8_t* packed, int64_t ldb, const float* norms, i
                        int bits, int precision, const float* qrot, int nq, const float* cent, int K,
                        int64_t row_offset, void* ws, size_t ws_bytes, cudaStream_t st,
                        float** parts_s, long long** parts_id, int* nparts) {
-  const int slots = pair_slots();
+  const int slots = pair_covers(n, bits) ? pair_slots() : 0;
   if (slots < 1)
     return run_batched_1cta(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent, K,
                             row_offset, ws, ws_bytes, st, parts_s, parts_id, nparts);
@@ -537,6 +587,20 @@ static int run_batched(const uint8_t* packed, int64_t ldb, const float* norms, i
   int rc;
   if ((rc = make_map(&mhi, w.qhi, b.nq_pad, b.ldk, kPM))) return rc;
   if ((rc = make_map(&mlo, w.qlo, b.nq_pad, b.ldk, kPM))) return rc;
+  CUtensorMap mraw;
+  {
+    auto fn = get_encode_fn();
+    if (!fn) return fail(PQ_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)ldb, (cuuint64_t)n};
+    cuuint64_t strides[1] = {(cuuint64_t)ldb};
+    cuuint32_t box[2] = {(cuuint32_t)(8 * bits), (cuuint32_t)kPNh};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(&mraw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(packed), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return fail(PQ_ERR_CUDA, "cuTensorMapEncodeTiled (code tiles) failed (%d)", (int)r);
+  }
   BatArgs a;
   a.packed = packed; a.ldb = ldb; a.norms = norms; a.n = n; a.d = d; a.nk = b.nk;
   a.shift = bits - precision; a.nq = nq; a.qtiles = b.qtiles; a.rchunks = b.rchunks;
@@ -552,11 +616,9 @@ static int run_batched(const uint8_t* packed, int64_t ldb, const float* norms, i
     auto kern = pair_adc_kernel<BB>;                                                            \
     PQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,        \
                                      (int)b.smem));                                             \
-    PQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, mhi, mlo, a));                                   \
+    PQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, mhi, mlo, mraw, a));                                   \
   } break;
-    PQ_PAIR_CASE(1)
     PQ_PAIR_CASE(2)
-    PQ_PAIR_CASE(3)
     PQ_PAIR_CASE(4)
     PQ_PAIR_CASE(8)
 #undef PQ_PAIR_CASE
@@ -573,7 +635,7 @@ static int run_batched(const uint8_t* packed, int64_t ldb, const float* norms, i
 static size_t batched_ws(int64_t n, int d, int nq, int k) {
   if (n <= 0 || nq <= 0 || k <= 0 || d <= 0) return 256;
   const size_t one = batched_ws_1cta(n, d, nq, k);
-  const int slots = pair_slots();
+  const int slots = pair_slots();  // any width: the workspace does not depend on it
   if (slots < 1) return one;
   const PairPlan b = pair_plan(n, d, nq, k, slots);
   BatWs w;

@@ -344,7 +344,7 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
         __syncwarp();
         tc::tmem_ld16(taddr + (uint32_t)c0, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
         tc::tmem_ld16(taddr + (uint32_t)c0 + 16u, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
-        tc::tmem_ld_wait();
+        tc::tmem_ld_wait(v);
         const int col0 = nb * BN + c0;
         if (col0 >= d) continue;  // warp-uniform
         if constexpr (BITS == 0) {

@@ -146,8 +146,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
-__device__ __forceinline__ void tmem_ld_wait() {
+// Waits for this thread's outstanding tcgen05.ld and pins the loaded
+// registers behind the wait: their values are defined only after
+// tcgen05.wait::ld, and without the register dependency the compiler may move
+// arithmetic on them above the wait (reading registers the load has not yet
+// written).
+template <int N>
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[N]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
 }
 
 // Shared-memory descriptor of a K-major, 128-byte-swizzled tile whose rows

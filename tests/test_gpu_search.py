@@ -315,3 +315,17 @@ def test_batched_adc_full_query_tiles(gpu, bits):
     bad = sum(not O.topk_equal_up_to_ties(GI[q], GS[q], RI[q], RS[q], rtol=RTOL)
               for q in range(len(qs)))
     assert bad == 0
+
+
+@pytest.mark.parametrize("bits,d,k", [(8, 768, 50), (4, 768, 200), (8, 256, 200)])
+def test_batched_adc_repeatable(gpu, bits, d, k):
+    """Repeated launches of the batched kernel agree with the streaming scan
+    every time (guards the producer/consumer hand-offs of the code-tile ring
+    and the accumulator buffers, whose failures are timing dependent)."""
+    pq, cv, idx, norms, qs = make_case(bits, d=d, n=5000, nq=129)
+    SI, SS = _batched(pq, cv, qs, k, None, "scan")
+    for rep in range(4):
+        GI, GS = _batched(pq, cv, qs, k, None, "batch")
+        bad = sum(not O.topk_equal_up_to_ties(GI[q], GS[q], SI[q], SS[q], rtol=RTOL)
+                  for q in range(len(qs)))
+        assert bad == 0, (rep, bad)
