@@ -7,6 +7,7 @@
 #include "encode.cu"
 #include "scan2.cu"
 #include "batched.cu"
+#include "batched_i8.cu"
 #include "batched2.cu"
 #include "ivf.cu"
 #include "noalloc.cu"

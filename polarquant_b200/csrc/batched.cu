@@ -766,11 +766,14 @@ int pq_adc_batch(const uint8_t* packed, int64_t ldb, const float* norms, int64_t
   cudaStream_t st = (cudaStream_t)stream;
   float* ps;
   long long* pi;
-  int parts;
-  rc = run_batched(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent, k, row_offset, ws,
-                   ws_bytes, st, &ps, &pi, &parts);
+  int parts, kpart = k;
+  rc = run_batched(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent, k, 0, ws, ws_bytes,
+                   st, &ps, &pi, &parts, &kpart);
   if (rc) return rc;
-  return launch_merge(ps, pi, parts, k, (long long)parts * k, k, nq, k, 0, out_scores,
+  if (kpart != k)
+    return rescore_candidates(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent, ps, pi,
+                              parts, kpart, k, row_offset, out_scores, (long long*)out_ids, st);
+  return launch_merge(ps, pi, parts, k, (long long)parts * k, k, nq, k, row_offset, out_scores,
                       (long long*)out_ids, st);
 }
 

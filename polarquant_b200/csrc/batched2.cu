@@ -562,7 +562,18 @@ using namespace pqb;
 static int run_batched(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
                        int bits, int precision, const float* qrot, int nq, const float* cent, int K,
                        int64_t row_offset, void* ws, size_t ws_bytes, cudaStream_t st,
-                       float** parts_s, long long** parts_id, int* nparts) {
+                       float** parts_s, long long** parts_id, int* nparts, int* kpart) {
+  *kpart = K;
+  if (i8_eligible(n, ldb, bits, K) &&
+      rerank_smem(d, precision, K + kI8Margin, K) <= 227 * 1024) {
+    const int s8 = i8_slots();
+    if (s8 >= 1) {
+      *kpart = K + kI8Margin;
+      return run_batched_i8(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent,
+                            K + kI8Margin, row_offset, ws, ws_bytes, st, s8, parts_s, parts_id,
+                            nparts);
+    }
+  }
   const int slots = pair_covers(n, bits) ? pair_slots() : 0;
   if (slots < 1)
     return run_batched_1cta(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent, K,
@@ -640,5 +651,7 @@ static size_t batched_ws(int64_t n, int d, int nq, int k) {
   const PairPlan b = pair_plan(n, d, nq, k, slots);
   BatWs w;
   const size_t two = pair_ws_carve(b, nq, k, nullptr, 0, &w);
-  return one > two ? one : two;
+  const size_t three = batched_i8_ws(n, d, nq, k);
+  const size_t m = one > two ? one : two;
+  return m > three ? m : three;
 }

@@ -228,7 +228,7 @@ int pq_ivf_search(const uint8_t* packed, int64_t ldb, const float* norms, int64_
                         k, 0, out_scores, (long long*)out_ids, st);
   const size_t smr = rerank_smem(d, bits, candidates, k);
   PQ_DISPATCH_B(bits, {
-    auto kern = rerank_kernel<B_>;
+    auto kern = rerank_kernel<B_, B_>;
     rc = set_smem(kern, smr);
     if (rc) return rc;
     kern<<<nq, kScanThreads, smr, st>>>(packed, ldb, norms, n, d, qrot, cent_full, cs, ci, parts,

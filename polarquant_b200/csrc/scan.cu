@@ -81,10 +81,11 @@ merge_topk_kernel(const float* __restrict__ in_s, const long long* __restrict__ 
   tk.write(out_s + (size_t)q * K, out_id + (size_t)q * K, id_offset);
 }
 
-// Full-precision rescoring of a candidate row list, then top-K.  When
-// `coarse` is non-null the list is first selected as the top-C of the coarse
-// per-block candidates (two-stage search, one block per query).
-template <int B>
+// Rescoring of a candidate row list at precision P (exact f32 table sums,
+// P = B: full precision), then top-K.  When `coarse` is non-null the list is
+// first selected as the top-C of the per-part candidate lists (two-stage
+// search, or the candidates of the int8 batched kernel), one block per query.
+template <int B, int P>
 __global__ void __launch_bounds__(kScanThreads)
 rerank_kernel(const uint8_t* __restrict__ packed, int64_t ldb, const float* __restrict__ norms,
               int64_t n, int d, const float* __restrict__ qrot, const float* __restrict__ cent_full,
@@ -93,7 +94,7 @@ rerank_kernel(const uint8_t* __restrict__ packed, int64_t ldb, const float* __re
               long long id_offset, float* __restrict__ out_s, long long* __restrict__ out_id) {
   extern __shared__ __align__(16) char smem[];
   const int q = blockIdx.x;
-  const size_t st_floats = query_state_floats<B>(d);
+  const size_t st_floats = query_state_floats<P>(d);
   float* st = reinterpret_cast<float*>(smem);
   long long* rows = reinterpret_cast<long long*>(smem + align_up(st_floats * sizeof(float), 16));
   char* tk_mem = reinterpret_cast<char*>(rows + align_up((size_t)C, 2));
@@ -128,7 +129,7 @@ rerank_kernel(const uint8_t* __restrict__ packed, int64_t ldb, const float* __re
     }
     nrows = C;
   }
-  build_query_state<B>(qrot + (size_t)q * d, d, cent_full, st, st, st + d);
+  build_query_state<P>(qrot + (size_t)q * d, d, cent_full, st, st, st + d);
   __syncthreads();
   tk.init(tk_mem, K, BlockTopK::cap_for(K, blockDim.x));
   const int lane = threadIdx.x & 31;
@@ -138,7 +139,7 @@ rerank_kernel(const uint8_t* __restrict__ packed, int64_t ldb, const float* __re
     if (i < nrows) r = rows[i];
     const bool valid = r >= 0 && r < n;
     float sc = 0.f;
-    if (valid) sc = score_row<B, B>(packed + r * ldb, d, st, st, st + d, lane) * __ldg(norms + r);
+    if (valid) sc = score_row<B, P>(packed + r * ldb, d, st, st, st + d, lane) * __ldg(norms + r);
     tk.offer(valid, sc, r);
     tk.end_round();
   }
@@ -307,10 +308,16 @@ static int run_scan(const uint8_t* packed, int64_t ldb, const float* norms, int6
   return PQ_OK;
 }
 
+// Batched ADC (tensor cores): per-(query, row chunk) candidate lists of
+// *kpart entries each in ws, layout [nq][*nparts][*kpart], ids local (+
+// row_offset).  *kpart == K: the lists hold exact scores and the top-K of each
+// chunk.  *kpart > K: the lists hold the top-*kpart of each chunk by an
+// approximate score (int8 kernel); rescore_candidates() then gives the exact
+// top-K.
 static int run_batched(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
                        int bits, int precision, const float* qrot, int nq, const float* cent, int K,
                        int64_t row_offset, void* ws, size_t ws_bytes, cudaStream_t st,
-                       float** parts_s, long long** parts_id, int* nparts);
+                       float** parts_s, long long** parts_id, int* nparts, int* kpart);
 
 static int adc_large_k(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
                        int bits, int precision, const float* qrot, int nq, const float* cent,
@@ -369,19 +376,50 @@ constexpr int kTwostageBatchMin = 64;
 
 static size_t batched_ws(int64_t n, int d, int nq, int k);
 
+// Offset of the exact coarse candidates (nq x candidates scores + ids) that
+// follow the batched workspace in two-stage search.
+static size_t twostage_exact_offset(int64_t n, int d, int nq, int candidates) {
+  return align_up(batched_ws(n, d, nq, candidates), 256);
+}
+
 size_t pq_twostage_workspace_bytes(int64_t n, int d, int nq, int candidates) {
   const size_t a = pq_adc_scan_workspace_bytes(n, d, nq, candidates);
   if (nq >= kTwostageBatchMin && candidates <= 256) {
-    const size_t b = batched_ws(n, d, nq, candidates);
+    const size_t b = twostage_exact_offset(n, d, nq, candidates) +
+                     align_up((size_t)nq * candidates * sizeof(float), 256) +
+                     (size_t)nq * candidates * sizeof(long long) + 256;
     return a > b ? a : b;
   }
   return a;
 }
 
+// Shared memory of rerank_kernel<B, P> with `bits` = P.
 static size_t rerank_smem(int d, int bits, int C, int K) {
   const size_t st = (bits <= 4) ? (size_t)d * 16 : (size_t)d + (size_t)(1 << bits) * 32;
   const int cap = BlockTopK::cap_for(C > K ? C : K, kScanThreads);
   return align_up(st * 4, 16) + align_up((size_t)C, 2) * 8 + BlockTopK::smem_bytes(cap);
+}
+
+// Exact top-K of approximate candidate lists (layout [nq][parts][C], local
+// row ids): per query the top-C of all lists by the approximate score, each
+// rescored at precision P with the f32 table sums of the streaming scan,
+// then the top-K; output ids + id_offset.
+static int rescore_candidates(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n,
+                              int d, int bits, int precision, const float* qrot, int nq,
+                              const float* cent, const float* cs, const long long* ci, int parts,
+                              int C, int K, int64_t id_offset, float* out_s, long long* out_id,
+                              cudaStream_t st) {
+  const size_t sm = rerank_smem(d, precision, C, K);
+  int rc = PQ_OK;
+  PQ_DISPATCH_BP(bits, precision, {
+    auto kern = rerank_kernel<B_, P_>;
+    rc = set_smem(kern, sm);
+    if (rc) return rc;
+    kern<<<nq, kScanThreads, sm, st>>>(packed, ldb, norms, n, d, qrot, cent, cs, ci, parts,
+                                       nullptr, C, K, id_offset, out_s, out_id);
+  });
+  PQ_LAUNCH_CHECK("rerank_kernel");
+  return PQ_OK;
 }
 
 int pq_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d, int bits,
@@ -405,8 +443,31 @@ int pq_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
   long long* ci;
   int nblk;
   if (nq >= kTwostageBatchMin && candidates <= 256) {
+    int kpart = candidates;
     rc = run_batched(packed, ldb, norms, n, d, bits, coarse_precision, qrot, nq, cent_coarse,
-                     candidates, 0, ws, ws_bytes, st, &cs, &ci, &nblk);
+                     candidates, 0, ws, ws_bytes, st, &cs, &ci, &nblk, &kpart);
+    if (rc) return rc;
+    if (kpart != candidates) {
+      // Approximate coarse lists: exact coarse scores of the best kpart, top
+      // `candidates` of them (global ids), then the full-precision rerank.
+      float* es = reinterpret_cast<float*>((char*)ws + twostage_exact_offset(n, d, nq, candidates));
+      long long* ei = reinterpret_cast<long long*>(
+          (char*)es + align_up((size_t)nq * candidates * sizeof(float), 256));
+      rc = rescore_candidates(packed, ldb, norms, n, d, bits, coarse_precision, qrot, nq,
+                              cent_coarse, cs, ci, nblk, kpart, candidates, row_offset, es, ei, st);
+      if (rc) return rc;
+      const size_t sm = rerank_smem(d, bits, candidates, k);
+      PQ_DISPATCH_B(bits, {
+        auto kern = rerank_kernel<B_, B_>;
+        rc = set_smem(kern, sm);
+        if (rc) return rc;
+        kern<<<nq, kScanThreads, sm, st>>>(packed, ldb, norms, n, d, qrot, cent_full, nullptr,
+                                           nullptr, 0, ei, candidates, k, row_offset, out_scores,
+                                           (long long*)out_ids);
+      });
+      PQ_LAUNCH_CHECK("rerank_kernel");
+      return PQ_OK;
+    }
   } else {
     nblk = scan_blocks(n, nq);
     Carve cv(ws, ws_bytes);
@@ -419,7 +480,7 @@ int pq_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
   if (rc) return rc;
   const size_t sm = rerank_smem(d, bits, candidates, k);
   PQ_DISPATCH_B(bits, {
-    auto kern = rerank_kernel<B_>;
+    auto kern = rerank_kernel<B_, B_>;
     rc = set_smem(kern, sm);
     if (rc) return rc;
     kern<<<nq, kScanThreads, sm, st>>>(packed, ldb, norms, n, d, qrot, cent_full, cs, ci, nblk,
@@ -444,7 +505,7 @@ int pq_rerank(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n,
   const size_t sm = align_up(st_f * 4, 16) + align_up((size_t)C, 2) * 8 +
                     BlockTopK::smem_bytes(BlockTopK::cap_for(k, kScanThreads));
   PQ_DISPATCH_B(bits, {
-    auto kern = rerank_kernel<B_>;
+    auto kern = rerank_kernel<B_, B_>;
     rc = set_smem(kern, sm);
     if (rc) return rc;
     kern<<<nq, kScanThreads, sm, st>>>(packed, ldb, norms, n, d, qrot, cent_full, nullptr, nullptr,

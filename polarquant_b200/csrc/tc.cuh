@@ -255,6 +255,18 @@ __device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, u
       : "memory");
 }
 
+// Pair MMA on 8-bit integer operands (kind::i8, s32 accumulation), same
+// operand split across the two CTAs as mma_f16_pair.
+__device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on the mbarrier at offset `bar` in every CTA of `mask` when all
 // pair MMAs issued so far by this thread have completed.
 __device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint16_t mask) {
@@ -269,6 +281,14 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint16_t mask) {
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
   return (1u << 4)                      // D format f32
          | (0u << 7) | (0u << 10)       // A, B format f16
+         | ((uint32_t)(N >> 3) << 17)   // N / 8
+         | ((uint32_t)(M >> 4) << 24);  // M / 16
+}
+
+// Instruction descriptor, kind::i8: A = B = signed 8-bit, D = s32, both K-major.
+__host__ __device__ constexpr uint32_t idesc_i8_s32(int M, int N) {
+  return (2u << 4)                      // D format s32
+         | (1u << 7) | (1u << 10)       // A, B signed 8-bit
          | ((uint32_t)(N >> 3) << 17)   // N / 8
          | ((uint32_t)(M >> 4) << 24);  // M / 16
 }
