@@ -563,9 +563,12 @@ def main():
 
     # ---- dominant kernel ----------------------------------------------------
     # Batches of >= 64 queries run the per-rank ADC on the tensor cores
-    # (batched_adc_kernel, timed inside the steps above): bound = tensor,
-    # algorithmic work 2*nq*n_local*d flops per launch (each MAC counted once;
-    # the fp16 split issues three MMAs per MAC).
+    # (pq_adc_batch: pair_i8_kernel for 2/4/8-bit codes, then the exact
+    # rescoring of its candidates; timed inside the steps above, all of its
+    # launches): bound = tensor, algorithmic work 2*nq*n_local*d flops per call
+    # (each MAC counted once; the int8 split issues three int8 MMAs per MAC,
+    # against the measured dense bf16 peak -- the int8 pipe's nominal rate is
+    # twice that).
     hbm, bf16, peak_kind = measured_peaks()
     row_bytes = rows.row_bytes + 4
     if batched:
@@ -573,7 +576,8 @@ def main():
         ach = flops / (kms / 1e3) / 1e12
         roof = {"bound": "tensor", "achieved": ach, "peak": bf16, "unit": "TFLOP/s",
                 "frac": ach / bf16, "traffic": None,
-                "kernel": "batched_adc_kernel (tcgen05, fp16 hi/lo split: 3 MMAs per MAC)",
+                "kernel": "pair_i8_kernel (tcgen05 kind::i8 CTA pairs, 3 int8 MMAs per MAC) "
+                          "+ exact rescoring of K+32 candidates (whole pq_adc_batch call)",
                 "peak_kind": f"{peak_kind} dense bf16 (burst)",
                 "alg_flops_per_launch": flops, "launch_ms": kms}
     # The streaming single-query scan (pq_adc_scan) on the same corpus: HBM-bound.

@@ -57,6 +57,7 @@ struct BatArgs {
   float* out_s;           // [nq][rchunks][K]
   long long* out_id;
   long long row_offset;
+  unsigned int* gthr;     // int8 kernel: per-query running threshold (ordered key, 0 = none)
 };
 
 // Loads the 8 codes k0..k0+7 (k0 % 8 == 0) of a row as the low bits of c[].
@@ -213,16 +214,14 @@ __device__ __forceinline__ void warp_select(int src, int lane, int n_src, float*
     int c = 0;
 #pragma unroll
     for (int j = 0; j < PER; ++j) c += key[j] >= cand;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    c = (int)__reduce_add_sync(0xffffffffu, (unsigned)c);
     if (c >= K) prefix = cand;
   }
   // prefix = K-th largest key.  Keep key > prefix, then ties in buffer order.
   int above = 0;
 #pragma unroll
   for (int j = 0; j < PER; ++j) above += key[j] > prefix;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) above += __shfl_xor_sync(0xffffffffu, above, o);
+  above = (int)__reduce_add_sync(0xffffffffu, (unsigned)above);
   int ties_left = K - above;
   int out = 0;
 #pragma unroll
@@ -711,7 +710,7 @@ static int run_batched_1cta(const uint8_t* packed, int64_t ldb, const float* nor
   a.shift = bits - precision; a.nq = nq; a.qtiles = b.qtiles; a.rchunks = b.rchunks;
   a.rows_per_chunk = b.rpc; a.K = K; a.cap = b.cap; a.qinv = w.qinv; a.cscale = w.cscale;
   a.lut = w.lut; a.lut_size = lut_size; a.buf_s = w.buf_s; a.buf_i = w.buf_i;
-  a.out_s = w.out_s; a.out_id = w.out_id; a.row_offset = row_offset;
+  a.out_s = w.out_s; a.out_id = w.out_id; a.row_offset = row_offset; a.gthr = nullptr;
   if (b.smem > 227 * 1024) return fail(PQ_ERR_UNSUPPORTED, "batched smem %zu too large", b.smem);
   switch (bits) {
 #define PQ_BAT_CASE(BB)                                                                         \

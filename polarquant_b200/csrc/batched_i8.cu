@@ -29,7 +29,9 @@
 // thread and PRMT looks up four codes at once (no shared-memory table, no
 // bank conflicts); the lookup yields each byte's two codes swapped, so the
 // query planes are stored with coordinates swapped in pairs to match (the dot
-// product is unchanged).  2- and 8-bit codes: a shared table of the 2^P digit
+// product is unchanged).  8-bit codes at precision <= 4 use the same register
+// tables after gathering four shifted codes into PRMT selector nibbles.  2-bit
+// codes and 8-bit codes at precision >= 5: a shared table of the 2^P digit
 // pairs indexed by the shifted code.
 //
 // Roles per CTA (480 threads): warp 0 loads this CTA's query planes by TMA
@@ -91,9 +93,29 @@ __device__ __forceinline__ void nib_lookup(const uint32_t (&T)[4], uint32_t s, u
   o1 = (prmt(T[0], T[1], s1) & ~m1) | (prmt(T[2], T[3], s1) & m1);
 }
 
+// Inverse of ordered_key() for keys != 0.
+__device__ __forceinline__ float key_to_float(unsigned k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
 // bar.sync on named barrier `id` for `count` threads (whole warps).
 __device__ __forceinline__ void named_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Four 8-bit codes of word w (one per byte, in K order) shifted down to a
+// precision P <= 4 (shift = 8 - P, mask = 2^P - 1 in every byte) and looked
+// up in the same register tables: the codes are gathered into the four
+// selector nibbles, bytes returned in K order.
+__device__ __forceinline__ void byte_lookup(uint32_t w, int shift, uint32_t mask,
+                                            const uint32_t (&TH)[4], const uint32_t (&TL)[4],
+                                            uint32_t& h, uint32_t& l) {
+  const uint32_t t = (w >> shift) & mask;      // code k in the low nibble of byte k
+  const uint32_t u = t | (t >> 4);             // byte 0 = c0 | c1 << 4, byte 2 = c2 | c3 << 4
+  const uint32_t s = prmt(u, 0u, 0x0020u) & 0x7777u;
+  const uint32_t m = prmt(t << 4, 0u, 0xBA98u);  // byte k = sign of code k's top bit
+  h = (prmt(TH[0], TH[1], s) & ~m) | (prmt(TH[2], TH[3], s) & m);
+  l = (prmt(TL[0], TL[1], s) & ~m) | (prmt(TL[2], TL[3], s) & m);
 }
 
 struct PairWalkI8 {
@@ -331,8 +353,10 @@ pair_i8_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant_
     // swizzled hi/lo planes.  Rows past the chunk decode to finite digits and
     // are ignored by the epilogue.
     const int dt = threadIdx.x - 10 * 32;
-    uint32_t TH[4], TL[4];
-    if constexpr (B == 4) {
+    uint32_t TH[4] = {0u, 0u, 0u, 0u}, TL[4] = {0u, 0u, 0u, 0u};
+    const bool regs = (B == 4) || (B == 8 && p.shift >= 4);  // register-table decode
+    const uint32_t bmask = ((1u << (8 - p.shift)) - 1u) * 0x01010101u;
+    if (regs) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         TH[i] = p.lut[256 + i];
@@ -376,6 +400,10 @@ pair_i8_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant_
               nib_lookup(TH, sel, m0, m1, hw[2 * j], hw[2 * j + 1]);
               nib_lookup(TL, sel, m0, m1, lw[2 * j], lw[2 * j + 1]);
             }
+          } else if (B == 8 && regs) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+              byte_lookup(cur[i][g], p.shift, bmask, TH, TL, hw[g], lw[g]);
           } else {
 #pragma unroll
             for (int g = 0; g < 4; ++g) {
@@ -443,64 +471,99 @@ pair_i8_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant_
       // then fails at once) so that both halves still meet at each named
       // barrier below.
       for (int tile = 0; tile < tiles; ++tile, ++tcount) {
+        const int64_t hr0 = r0 + (int64_t)tile * kQN + half * (kQN / 2);  // this half's rows
+        // The half's 128 norms, loaded before the accumulator wait (which
+        // hides their latency): register c holds row hr0 + 32 c + lane.
+        float nrm[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int64_t row = hr0 + 32 * c + lane;
+          nrm[c] = (ok && row < r1) ? __ldg(p.norms + row) : 0.f;
+        }
+        const unsigned gkey = (ok && qv) ? __ldcg(p.gthr + qg) : 0u;
+        // Norm range of each 16-row group, also before the wait: after the
+        // reduction lanes 0-15 of register c hold group 2c's, lanes 16-31
+        // group 2c+1's.
+        float nmx[4], nmn[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          nmx[c] = nrm[c];
+          nmn[c] = nrm[c];
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) {
+            nmx[c] = fmaxf(nmx[c], __shfl_xor_sync(0xffffffffu, nmx[c], o));
+            nmn[c] = fminf(nmn[c], __shfl_xor_sync(0xffffffffu, nmn[c], o));
+          }
+        }
         if (ok && !tc::mbar_wait(bar(TFULL), (uint32_t)tcount & 1u, abort_flag,
                                  tc::kErrWaitAccFull))
           ok = false;
         ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
         if (!ok) continue;
         tc::tc_fence_after();
-        const int64_t tr0 = r0 + (int64_t)tile * kQN;
-        const uint32_t taddr = tmem_base + ((uint32_t)(32 * quad) << 16);
-        for (int c0 = half * (kQN / 2); c0 < (half + 1) * (kQN / 2); c0 += 32) {
+        // The best threshold any task of this query has published: at least
+        // K approximate scores (in some row chunk) reach it, so rows below it
+        // cannot enter the query's overall top K.
+        if (gkey != 0u) thr = fmaxf(thr, key_to_float(gkey));
+        const uint32_t taddr =
+            tmem_base + ((uint32_t)(32 * quad) << 16) + (uint32_t)(half * (kQN / 2));
+        // 16-column groups g = 0..7 of the half.
+#pragma unroll 1
+        for (int g = 0; g < 8; ++g) {
+          uint32_t h[16], x[16];
           __syncwarp();
-          uint32_t need = __ballot_sync(0xffffffffu, qv && cnt + 32 > p.cap);
-          while (need) {
-            const int src = __ffs(need) - 1;
-            need &= need - 1;
-            warp_select(src, lane, cnt, p.buf_s + buf_of(32 * quad + src),
-                        p.buf_i + buf_of(32 * quad + src), p.K, cnt, thr);
+          tc::tmem_ld16(taddr + (uint32_t)(16 * g), h);
+          tc::tmem_ld16(taddr + (uint32_t)(kQN + 16 * g), x);
+          tc::tmem_ld_wait(h);
+          tc::tmem_ld_wait(x);
+          if ((g & 1) == 0) {
+            // Room for 32 more candidates in every buffer of the warp.
+            uint32_t need = __ballot_sync(0xffffffffu, qv && cnt + 32 > p.cap);
+            while (need) {
+              const int src = __ffs(need) - 1;
+              need &= need - 1;
+              const float before = thr;
+              warp_select(src, lane, cnt, p.buf_s + buf_of(32 * quad + src),
+                          p.buf_i + buf_of(32 * quad + src), p.K, cnt, thr);
+              if (lane == src) {
+                thr = fmaxf(thr, before);  // never below a threshold already adopted
+                atomicMax(p.gthr + qg, ordered_key(thr));  // publish
+              }
+            }
           }
-          const int64_t rb = tr0 + c0;
-          // The 32 rows' norms (0 past the chunk) and, per 16-row group, their
-          // max and min, reduced across the lanes holding them.
-          const float my_norm = (rb + lane < r1) ? __ldg(p.norms + rb + lane) : 0.f;
-          float nmax = my_norm, nmin = my_norm;
+          const int c = g >> 1;                       // rows of groups 2c, 2c + 1
+          const float nr_all = c == 0 ? nrm[0] : c == 1 ? nrm[1] : c == 2 ? nrm[2] : nrm[3];
+          const float gmax = __shfl_sync(
+              0xffffffffu, c == 0 ? nmx[0] : c == 1 ? nmx[1] : c == 2 ? nmx[2] : nmx[3],
+              16 * (g & 1));
+          const float gmin = __shfl_sync(
+              0xffffffffu, c == 0 ? nmn[0] : c == 1 ? nmn[1] : c == 2 ? nmn[2] : nmn[3],
+              16 * (g & 1));
+          int t8[8];                                   // tree max of the 16 combined values
 #pragma unroll
-          for (int o = 8; o > 0; o >>= 1) {
-            nmax = fmaxf(nmax, __shfl_xor_sync(0xffffffffu, nmax, o));
-            nmin = fminf(nmin, __shfl_xor_sync(0xffffffffu, nmin, o));
-          }
+          for (int i = 0; i < 8; ++i)
+            t8[i] = max((int)h[i] + (((int)x[i] + 128) >> 8),
+                        (int)h[i + 8] + (((int)x[i + 8] + 128) >> 8));
 #pragma unroll
-          for (int g = 0; g < 2; ++g) {
-            uint32_t h[16], x[16];
-            __syncwarp();
-            tc::tmem_ld16(taddr + (uint32_t)(c0 + 16 * g), h);
-            tc::tmem_ld16(taddr + (uint32_t)(kQN + c0 + 16 * g), x);
-            tc::tmem_ld_wait(h);
-            tc::tmem_ld_wait(x);
-            const float gmax = __shfl_sync(0xffffffffu, nmax, 16 * g);
-            const float gmin = __shfl_sync(0xffffffffu, nmin, 16 * g);
-            int v[16];
-            int vmax = (int)0x80000000;
+          for (int i = 0; i < 4; ++i) t8[i] = max(t8[i], t8[i + 4]);
+          const int vmax = max(max(t8[0], t8[2]), max(t8[1], t8[3]));
+          const float bound = (__int2float_rn(vmax) * qs) * (vmax >= 0 ? gmax : gmin);
+          const bool want = qv && bound > thr;
+          if (__any_sync(0xffffffffu, want)) {
+            // Every row of the group scored; passing rows appended with
+            // predicated stores (no per-row branch).
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              v[i] = (int)h[i] + (((int)x[i] + 128) >> 8);
-              vmax = max(vmax, v[i]);
-            }
-            const float bound = (__int2float_rn(vmax) * qs) * (vmax >= 0 ? gmax : gmin);
-            if (qv && bound > thr) {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const int64_t row = rb + 16 * g + i;
-                if (row < r1) {
-                  const float sc = (__int2float_rn(v[i]) * qs) * __ldg(p.norms + row);
-                  if (sc > thr) {
-                    bs[cnt] = sc;
-                    bi[cnt] = (int)row;
-                    ++cnt;
-                  }
-                }
+              const float nr = __shfl_sync(0xffffffffu, nr_all, 16 * (g & 1) + i);
+              const int64_t row = hr0 + 16 * g + i;
+              const int v = (int)h[i] + (((int)x[i] + 128) >> 8);
+              const float sc = (__int2float_rn(v) * qs) * nr;
+              const bool pass = want && row < r1 && sc > thr;
+              if (pass) {
+                bs[cnt] = sc;
+                bi[cnt] = (int)row;
               }
+              cnt += pass ? 1 : 0;
             }
           }
         }
@@ -580,10 +643,12 @@ qsplit_i8_kernel(const float* __restrict__ qrot, int nq, int d, int ldk, int swa
 }
 
 // Digit tables of the 2^P centroids: lut[c] = hi | lo << 8 (bytes) of
-// round(cent[c] * 32639 / max|cent|); lut[256..263] = the 4-bit decoder's
-// register tables (hi bytes, then lo bytes) of the 16 codes c -> cent[c >> shift];
+// round(cent[c] * 32639 / max|cent|); lut[256..263] = the register tables
+// (hi bytes, then lo bytes) of 16 entries c -> cent[c >> reg_shift] (0 past
+// the table): reg_shift = bits - P for 4-bit codes (indexed by the stored
+// code), 0 for 8-bit codes (indexed by the shifted code);
 // cscale[0] = max|cent| / 32639 * 65536.
-__global__ void lut_i8_kernel(const float* __restrict__ cent, int size, int shift,
+__global__ void lut_i8_kernel(const float* __restrict__ cent, int size, int reg_shift,
                               uint32_t* __restrict__ lut, float* __restrict__ cscale) {
   __shared__ float mx;
   __shared__ uint32_t ent[256];
@@ -607,9 +672,8 @@ __global__ void lut_i8_kernel(const float* __restrict__ cent, int size, int shif
     const int plane = threadIdx.x >> 2, wd = threadIdx.x & 3;
     uint32_t v = 0;
     for (int b = 0; b < 4; ++b) {
-      const int c = 4 * wd + b;
-      const int e = (c >> shift) < size ? (c >> shift) : 0;
-      v |= ((ent[e] >> (8 * plane)) & 255u) << (8 * b);
+      const int e = (4 * wd + b) >> reg_shift;
+      if (e < size) v |= ((ent[e] >> (8 * plane)) & 255u) << (8 * b);
     }
     lut[256 + threadIdx.x] = v;
   }
@@ -723,6 +787,7 @@ struct I8Ws {
   int8_t *qhi, *qlo;
   float *qscale, *cscale, *buf_s, *out_s;
   uint32_t* lut;
+  unsigned int* gthr;
   int* buf_i;
   long long* out_id;
 };
@@ -734,6 +799,7 @@ static size_t i8_ws_carve(const I8Plan& b, int nq, int K, void* ws, size_t ws_by
   w->qscale = cv.take<float>((size_t)b.nq_pad);
   w->cscale = cv.take<float>(4);
   w->lut = cv.take<uint32_t>(256 + 8);
+  w->gthr = cv.take<unsigned int>((size_t)b.nq_pad);
   w->buf_s = cv.take<float>((size_t)b.grid * kQM * 2 * b.cap);
   w->buf_i = cv.take<int>((size_t)b.grid * kQM * 2 * b.cap);
   w->out_s = cv.take<float>((size_t)nq * 2 * b.rchunks * K);
@@ -777,6 +843,7 @@ static int run_batched_i8(const uint8_t* packed, int64_t ldb, const float* norms
   i8_ws_carve(b, nq, K, ws, ws_bytes, &w);
   PQ_CUDA_TRY(cudaMemsetAsync(w.qhi, 0, (size_t)b.nq_pad * b.ldk, st));
   PQ_CUDA_TRY(cudaMemsetAsync(w.qlo, 0, (size_t)b.nq_pad * b.ldk, st));
+  PQ_CUDA_TRY(cudaMemsetAsync(w.gthr, 0, (size_t)b.nq_pad * sizeof(unsigned int), st));
   {
     const int pg = (nq + 7) / 8 < num_sms() * 16 ? (nq + 7) / 8 : num_sms() * 16;
     qsplit_i8_kernel<<<pg, 256, 0, st>>>(qrot, nq, d, b.ldk, bits == 4 ? 1 : 0, w.qhi, w.qlo,
@@ -784,7 +851,8 @@ static int run_batched_i8(const uint8_t* packed, int64_t ldb, const float* norms
     PQ_LAUNCH_CHECK("qsplit_i8_kernel");
   }
   const int lut_size = 1 << precision;
-  lut_i8_kernel<<<1, 256, 0, st>>>(cent, lut_size, bits - precision, w.lut, w.cscale);
+  lut_i8_kernel<<<1, 256, 0, st>>>(cent, lut_size, bits == 4 ? bits - precision : 0, w.lut,
+                                   w.cscale);
   PQ_LAUNCH_CHECK("lut_i8_kernel");
   CUtensorMap mhi, mlo, mraw;
   int rc;
@@ -796,7 +864,7 @@ static int run_batched_i8(const uint8_t* packed, int64_t ldb, const float* norms
   a.shift = bits - precision; a.nq = nq; a.qtiles = b.qtiles; a.rchunks = b.rchunks;
   a.rows_per_chunk = b.rpc; a.K = K; a.cap = b.cap; a.qinv = w.qscale; a.cscale = w.cscale;
   a.lut = w.lut; a.lut_size = lut_size; a.buf_s = w.buf_s; a.buf_i = w.buf_i;
-  a.out_s = w.out_s; a.out_id = w.out_id; a.row_offset = row_offset;
+  a.out_s = w.out_s; a.out_id = w.out_id; a.row_offset = row_offset; a.gthr = w.gthr;
   cudaLaunchConfig_t cfg;
   cudaLaunchAttribute at[1];
   i8_config(&cfg, at, b.grid, b.smem, st);
