@@ -80,6 +80,14 @@ WORKLOADS = {
 
 CHUNK = 65536
 
+# DRAM bytes (read + write) per launch of the dominant batched-ADC kernel from
+# the ncu capture of the 4M-row slice of the d=1536 workload at 10,000
+# queries (profiles/pair_i8_kernel_c4s.md: 25.2 GB read + 2.1 GB written),
+# scaled to other row counts of the same workload by rows (traffic grows with
+# the row tiles at a fixed query batch).
+PROFILED_TRAFFIC = {"rows": 4_000_000, "bytes": 27.29e9, "queries": 10_000, "d": 1536,
+                    "source": "profiles/pair_i8_kernel_c4s.md (4M-row capture, scaled by rows)"}
+
 
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
@@ -379,12 +387,16 @@ def main():
     ap.add_argument("--path", default="auto", choices=["auto", "scan", "batch"],
                     help="force the streaming scan or the tensor-core batch path")
     ap.add_argument("--queries", type=int, default=0, help="override the query count")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="override the corpus row count (small cases for ncu captures)")
     ap.add_argument("--quick", action="store_true",
                     help="timed steps only (no e2e, scan roofline or CPU baseline); for profiling")
     args = ap.parse_args()
     cfg = dict(WORKLOADS[args.workload])
     if args.queries:
         cfg["nq"] = args.queries
+    if args.rows:
+        cfg["n"] = args.rows
 
     import torch
     import torch.distributed as dist
@@ -574,8 +586,12 @@ def main():
     if batched:
         flops = 2.0 * cfg["nq"] * rows.n * cfg["d"]
         ach = flops / (kms / 1e3) / 1e12
+        pt = PROFILED_TRAFFIC
+        same = (cfg["d"] == pt["d"] and cfg["nq"] == pt["queries"] and cfg["bits"] == 4)
+        traffic = pt["bytes"] * rows.n / pt["rows"] if same else None
         roof = {"bound": "tensor", "achieved": ach, "peak": bf16, "unit": "TFLOP/s",
-                "frac": ach / bf16, "traffic": None,
+                "frac": ach / bf16, "traffic": traffic,
+                "traffic_source": pt["source"] if same else None,
                 "kernel": "pair_i8_kernel (tcgen05 kind::i8 CTA pairs, 3 int8 MMAs per MAC) "
                           "+ exact rescoring of K+32 candidates (whole pq_adc_batch call)",
                 "peak_kind": f"{peak_kind} dense bf16 (burst)",
