@@ -32,7 +32,7 @@ namespace pqb {
 
 constexpr int kEncBM = 128;     // rows per tile (TMEM lanes)
 constexpr int kEncBK = 64;      // K per stage: one 128-byte swizzle atom of fp16
-constexpr int kEncThreads = 192;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 epilogue
+constexpr int kEncThreads = 320;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 epilogue
 constexpr int kScaleBias = 14;  // R planes hold R * 2^14
 
 struct EncShape {
@@ -44,7 +44,9 @@ static EncShape enc_shape(int d) {
   EncShape s;
   s.d = d;
   s.ntn = (d + 255) / 256;
-  s.BN = ((d + s.ntn - 1) / s.ntn + 15) / 16 * 16;
+  // A multiple of 32: the epilogue packs 32 codes at a time, and a chunk
+  // must not run into the next column tile's bytes.
+  s.BN = ((d + s.ntn - 1) / s.ntn + 31) / 32 * 32;
   s.ldn = s.ntn * s.BN;
   s.ldk = (d + kEncBK - 1) / kEncBK * kEncBK;
   s.nk = s.ldk / kEncBK;
@@ -231,7 +233,7 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(bar(TFULL + b), 1);
-      tc::mbar_init(bar(TEMPTY + b), 4);
+      tc::mbar_init(bar(TEMPTY + b), 8);
     }
     tc::mbar_init(bar(DRAIN), 1);
     *abort_flag = 0;
@@ -326,8 +328,12 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
       tc::mbar_wait(bar(DRAIN), 0, &never, tc::kErrWaitAccFull);
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    const int q = warp & 3;
+    // ---------------- epilogue (warps 2..9) ----------------
+    // Warps w and w + 4 read the same TMEM lanes (rows), w the first half of
+    // the tile's BN columns and w + 4 the second.  Thread = row.
+    const int q = warp & 3, half = (warp - 2) >> 2;
+    const int nch = BN / 32, nch0 = (nch + 1) / 2;  // 32-column chunks, first half's share
+    const int cbeg = half ? 32 * nch0 : 0, cend = half ? BN : 32 * nch0;
     int tcount = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tcount) {
       const int mb = tile / ntn, nb = tile % ntn;
@@ -339,7 +345,7 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
       const bool rv = row < m;
       const float inv = rv ? __ldg(inv_scale + row) : 0.f;
       const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * BN);
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = cbeg; c0 < cend; c0 += 32) {
         uint32_t v[32];
         __syncwarp();
         tc::tmem_ld16(taddr + (uint32_t)c0, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
@@ -355,17 +361,28 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
               if (col0 + i < d) yr[col0 + i] = __uint_as_float(v[i]) * inv;
           }
         } else {
+          // np.searchsorted(boundaries, x, side='left') for the 32 values,
+          // step-major so the 32 table lookups of a step are independent.
+          float x[32];
           uint32_t c[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            x[i] = __uint_as_float(v[i]) * inv;
+            c[i] = 0;
+          }
+#pragma unroll
+          for (int step = 1 << (BITS - 1); step > 0; step >>= 1) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (x[i] > sb[c[i] + step - 1]) c[i] += step;
+          }
           uint32_t near = 0;
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            uint32_t cc = 0;
-            if (rv && col0 + i < d) {
-              const float x = __uint_as_float(v[i]) * inv;
-              cc = code_of<BITS>(x, sb);
-              if (near_boundary<BITS>(x, cc, sb)) near |= 1u << i;
-            }
-            c[i] = cc;
+            if (isnan(x[i])) c[i] = (1u << BITS) - 1u;  // NaN sorts last, as in NumPy
+            const bool valid = rv && col0 + i < d;
+            if (!valid) c[i] = 0;
+            else if (near_boundary<BITS>(x[i], c[i], sb)) near |= 1u << i;
           }
           // Coordinates within kFixBand of a boundary: the warp recomputes the
           // dot product in f64 from the exact f32 R and the 22-bit x planes,
@@ -390,8 +407,8 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
                           acc);
 #pragma unroll
               for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-              const float x = (float)(acc * ((double)sinv * (double)(1 << kScaleBias)));
-              const uint32_t code = code_of<BITS>(x, sb);
+              const float xr = (float)(acc * ((double)sinv * (double)(1 << kScaleBias)));
+              const uint32_t code = code_of<BITS>(xr, sb);
               if (lane == src) {
 #pragma unroll
                 for (int t = 0; t < 32; ++t)
@@ -405,9 +422,19 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
           uint8_t* dst = packed + (int64_t)row * ldb + (int64_t)col0 * BITS / 8;
           const int64_t off0 = (int64_t)col0 * BITS / 8;
           if (off0 + 4 * BITS <= rb) {
-            uint32_t* dw = reinterpret_cast<uint32_t*>(dst);
+            // 4*BITS bytes at a multiple of 4*BITS (col0 % 32 == 0, ldb % 16 == 0).
+            if constexpr (BITS == 4 || BITS == 8) {
+              uint4* dq = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-            for (int i = 0; i < BITS; ++i) dw[i] = w[i];
+              for (int i = 0; i < BITS / 4; ++i)
+                dq[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            } else if constexpr (BITS == 2) {
+              *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+            } else {
+              uint32_t* dw = reinterpret_cast<uint32_t*>(dst);
+#pragma unroll
+              for (int i = 0; i < BITS; ++i) dw[i] = w[i];
+            }
           } else {
             for (int i = 0; i < 4 * BITS && off0 + i < rb; ++i)
               dst[i] = (uint8_t)(w[i >> 2] >> (8 * (i & 3)));

@@ -75,17 +75,21 @@ def test_encode_d1024_lognormal_norms(gpu, bits):
     check_codes(cv.indices, ref, X, pq.R, pq.boundaries, bits)
 
 
-@pytest.mark.parametrize("d", [384, 768, 1536])
-def test_encode_other_dims(gpu, d):
+@pytest.mark.parametrize("d,bits", [(384, 4), (768, 4), (1536, 4), (600, 4), (600, 3),
+                                    (200, 8)])
+def test_encode_other_dims(gpu, d, bits):
+    """Dimensions whose rotation output is split over several column tiles,
+    including widths where a tile is not a whole number of 64 columns (d=600:
+    three tiles of 224 columns, the last one ragged)."""
     from polarquant_b200 import Quantizer
     n = 3000
     rng = np.random.default_rng(d)
     X = rng.standard_normal((n, d)).astype(np.float32)
-    pq = Quantizer(d, bits=4, seed=42)
+    pq = Quantizer(d, bits=bits, seed=42)
     cv = pq.encode(X)
     ref, norms = O.encode(X, pq.R, pq.boundaries)
     np.testing.assert_array_equal(cv.norms, norms)
-    check_codes(cv.indices, ref, X, pq.R, pq.boundaries, 4)
+    check_codes(cv.indices, ref, X, pq.R, pq.boundaries, bits)
 
 
 def test_encode_tile_edges_and_tensor_input(gpu):
