@@ -564,7 +564,7 @@ static int run_batched(const uint8_t* packed, int64_t ldb, const float* norms, i
                        int64_t row_offset, void* ws, size_t ws_bytes, cudaStream_t st,
                        float** parts_s, long long** parts_id, int* nparts, int* kpart) {
   *kpart = K;
-  if (i8_eligible(n, ldb, bits, K) &&
+  if (i8_eligible(n, d, ldb, bits, K) &&
       rerank_smem(d, precision, K + kI8Margin, K) <= 227 * 1024) {
     const int s8 = i8_slots();
     if (s8 >= 1) {

@@ -739,12 +739,20 @@ static int i8_slots() {
 // twice that error of it, i.e. inside the score-tie band.
 constexpr int kI8Margin = 32;
 
-// Shapes the int8 kernel takes: 2-, 4- and 8-bit codes, at least one pair
-// tile of rows, a row stride of at least one raw K block (the TMA box), and
-// K + margin within the epilogue's selection limit.
-static bool i8_eligible(int64_t n, int64_t ldb, int bits, int K) {
-  return (bits == 2 || bits == 4 || bits == 8) && n >= kQN && ldb >= kQBK * bits / 8 &&
-         K + kI8Margin <= kBatMaxK;
+// Smallest dimension for which the int8 kernel is used.  Its two
+// accumulators fill the TMEM, so a tile's epilogue (~7.5 k cycles with the
+// hand-offs) does not overlap the next tile's MMAs (~1.6 k cycles per 128 of
+// d); the fp16 pair kernel double-buffers its accumulator but needs twice the
+// MMA time.  Measured on the B200: int8 1.45x faster at d=1536 (4-bit), fp16
+// 1.2x faster at d=768 (8-bit codes at precision 4).
+constexpr int kI8MinDim = 1024;
+
+// Shapes the int8 kernel takes: 2-, 4- and 8-bit codes, d >= kI8MinDim, at
+// least one pair tile of rows, a row stride of at least one raw K block (the
+// TMA box), and K + margin within the epilogue's selection limit.
+static bool i8_eligible(int64_t n, int d, int64_t ldb, int bits, int K) {
+  return (bits == 2 || bits == 4 || bits == 8) && d >= kI8MinDim && n >= kQN &&
+         ldb >= kQBK * bits / 8 && K + kI8Margin <= kBatMaxK;
 }
 
 static I8Plan i8_plan(int64_t n, int d, int nq, int k, int slots, int bits) {
@@ -892,7 +900,7 @@ static int run_batched_i8(const uint8_t* packed, int64_t ldb, const float* norms
 }
 
 static size_t batched_i8_ws(int64_t n, int d, int nq, int k) {
-  if (k + kI8Margin > kBatMaxK || n < kQN) return 256;
+  if (k + kI8Margin > kBatMaxK || n < kQN || d < kI8MinDim) return 256;
   const int slots = i8_slots();
   if (slots < 1) return 256;
   const I8Plan b = i8_plan(n, d, nq, k + kI8Margin, slots, 4);

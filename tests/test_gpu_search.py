@@ -292,9 +292,14 @@ def test_search_batch_uses_tensor_cores_and_matches(gpu):
         assert_topk(a, b, c, e)
 
 
-@pytest.mark.parametrize("bits,cands,cp", [(8, 200, 4), (4, 100, 2), (8, 256, None)])
-def test_twostage_batched_coarse(gpu, bits, cands, cp):
-    pq, cv, idx, norms, qs = make_case(bits, d=128, n=5000, nq=80)
+@pytest.mark.parametrize("bits,cands,cp,d", [(8, 200, 4, 128), (4, 100, 2, 128),
+                                             (8, 256, None, 128), (8, 200, 4, 1024),
+                                             (4, 150, 2, 1024)])
+def test_twostage_batched_coarse(gpu, bits, cands, cp, d):
+    """Batched coarse stage (fp16 kernels at d=128; at d=1024 the int8 kernel,
+    whose candidates are rescored exactly at the coarse precision before the
+    full-precision rerank)."""
+    pq, cv, idx, norms, qs = make_case(bits, d=d, n=5000, nq=80)
     GI, GS = pq.search_twostage_many(cv, qs, k=10, candidates=cands, coarse_precision=cp)
     bad = 0
     for q in range(len(qs)):
@@ -304,14 +309,17 @@ def test_twostage_batched_coarse(gpu, bits, cands, cp):
     assert bad == 0
 
 
-@pytest.mark.parametrize("bits", [1, 2, 3, 4, 8])
-def test_batched_adc_full_query_tiles(gpu, bits):
+@pytest.mark.parametrize("d,bits", [(256, 1), (256, 2), (256, 3), (256, 4), (256, 8),
+                                    (1024, 2), (1024, 4), (1024, 8)])
+def test_batched_adc_full_query_tiles(gpu, d, bits):
     """Query batches spanning several 256-query tiles (both CTAs of each pair
-    busy) over many short row tiles (d=256: two K stages per tile), against the
-    oracle's search_batch, three launches in a row.  This shape exposed a
-    timing-dependent loss of candidate rows when a code-tile slot was handed
-    back to its TMA producer before the decoders had consumed it."""
-    pq, cv, idx, norms, qs = make_case(bits, d=256, n=40000, nq=520, data_seed=bits)
+    busy) over many row tiles and chunks, against the oracle's search_batch,
+    three launches in a row: d=256 runs the fp16 kernels, d=1024 the int8
+    kernel (2-, 4- and 8-bit codes).  These shapes exposed a timing-dependent
+    loss of candidate rows when a code-tile slot was handed back to its TMA
+    producer before the decoders had consumed it, and a race on the shared
+    sort scratch when a one-tile task followed."""
+    pq, cv, idx, norms, qs = make_case(bits, d=d, n=40000, nq=520, data_seed=bits)
     prec = max(1, bits - 1)
     RI, RS = O.search_batch(pq.R, pq.centroids, pq._nested, bits, idx, norms, qs, k=64,
                             precision=prec)
@@ -322,7 +330,8 @@ def test_batched_adc_full_query_tiles(gpu, bits):
         assert bad == 0, (rep, bad)
 
 
-@pytest.mark.parametrize("bits,d,k", [(8, 768, 50), (4, 768, 200), (8, 256, 200)])
+@pytest.mark.parametrize("bits,d,k", [(8, 768, 50), (4, 768, 200), (8, 256, 200),
+                                      (4, 1024, 100), (8, 1536, 64)])
 def test_batched_adc_repeatable(gpu, bits, d, k):
     """Repeated launches of the batched kernel agree with the streaming scan
     every time (guards the producer/consumer hand-offs of the code-tile ring
