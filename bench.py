@@ -627,7 +627,7 @@ def main():
         ibytes = visited * (row_bytes + 8)
         roof = {"bound": "hbm", "achieved": ibytes / (kms / 1e3) / 1e9, "peak": hbm,
                 "unit": "GB/s", "frac": ibytes / (kms / 1e3) / 1e9 / hbm, "traffic": None,
-                "kernel": "ivf_scan_kernel + rerank (whole pq_ivf_search call)",
+                "kernel": "ivf_group_scan_kernel + rerank (whole pq_ivf_search call)",
                 "peak_kind": peak_kind, "alg_bytes_per_launch": ibytes, "launch_ms": kms,
                 "rows_visited_per_query": visited / cfg["nq"]}
     elif not batched:

@@ -131,10 +131,14 @@ int pq_adc_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
 
 /* ---------------------------------------------------------------------------
  * Batched ADC on the tensor cores (tcgen05): scores of nq queries against
- * all n rows as one GEMM over decoded code tiles (fp16 hi/lo split, three
- * MMAs per K step, f32 accumulation), with the exact per-query top-k fused in
- * the epilogue.  Replaces Quantizer.search_batch (remex/core.py:721-778:
- * `Q_rot @ X_hat_rot.T * norms` and the per-row argpartition/argsort).
+ * all n rows as one GEMM over decoded code tiles.  Replaces
+ * Quantizer.search_batch (remex/core.py:721-778: `Q_rot @ X_hat_rot.T *
+ * norms` and the per-row argpartition/argsort).  For d >= 1024 and 2-, 4- or
+ * 8-bit codes (k <= 224) the GEMM runs on int8 digit planes of 16-bit fixed
+ * point and keeps the top k + 32 candidates per query, which are rescored
+ * with the f32 table sums of pq_adc_scan and cut to k; otherwise an fp16
+ * hi/lo split (three MMAs per K step, f32 accumulation) with the exact top-k
+ * fused in the epilogue.  Scores equal pq_adc_scan's up to f32 summation order.
  * Same arguments and output as pq_adc_scan; 1 <= k <= 256, k <= n.
  * ------------------------------------------------------------------------- */
 size_t pq_adc_batch_workspace_bytes(int64_t n, int d, int nq, int k);
@@ -204,9 +208,13 @@ int pq_rerank(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n,
  *   ADC scores over the probed cells' rows, remex/ivf.py:301-374) or
  *   .search_twostage (rerank = 1: top-`candidates` coarse rows, full-precision
  *   rescoring, top-k, remex/ivf.py:376-436).  sorted_idx/offsets: the CSR
- *   layout (rows grouped by cell, offsets n_cells + 1).  Each probed cell's
- *   rows are split over `splits` blocks.  Slots past a query's candidate count
- *   hold id -1.  Workspace: pq_ivf_workspace_bytes(nq, nprobe, splits, C).
+ *   layout (rows grouped by cell, offsets n_cells + 1).  cell_rows/cell_norms
+ *   (optional, both or neither): the packed rows (stride ldb, >= 64 bytes of
+ *   slack) and norms copied in CSR order, so each probed cell is read as one
+ *   contiguous run; without them rows are gathered through sorted_idx.  Each
+ *   query's probed rows are split into `splits` equal groups, one block and
+ *   one candidate list each.  Slots past a query's candidate count hold id -1.
+ *   Workspace: pq_ivf_workspace_bytes(nq, nprobe, splits, C).
  * ------------------------------------------------------------------------- */
 int pq_ivf_cell_ids(const uint8_t* packed, int64_t ldb, int64_t n, int d, int bits, int n_bits,
                     int mode, const float* hyperplanes, uint16_t* cells, void* stream);
@@ -217,8 +225,9 @@ int pq_ivf_search(const uint8_t* packed, int64_t ldb, const float* norms, int64_
                   int bits, int coarse_precision, const float* qrot, int nq,
                   const float* cent_coarse, const float* cent_full, int n_bits, int mode,
                   const float* hyperplanes, const int64_t* sorted_idx, const int64_t* offsets,
-                  int nprobe, int splits, int candidates, int k, int rerank, float* out_scores,
-                  int64_t* out_ids, void* ws, size_t ws_bytes, void* stream);
+                  const uint8_t* cell_rows, const float* cell_norms, int nprobe, int splits,
+                  int candidates, int k, int rerank, float* out_scores, int64_t* out_ids,
+                  void* ws, size_t ws_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Merge of per-part top-k lists: in_s/in_ids are parts x nq x kin (as written

@@ -51,8 +51,8 @@ SIGNATURES = {
     "pq_ivf_cell_ids": (_I, [_P, _L, _L, _I, _I, _I, _I, _P, _P, _P]),
     "pq_ivf_probe": (_I, [_P, _I, _I, _I, _I, _P, _I, _P, _P, _P]),
     "pq_ivf_workspace_bytes": (_Z, [_I, _I, _I, _I]),
-    "pq_ivf_search": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _I, _P, _P, _I, _I, _P, _P, _P, _I,
-                           _I, _I, _I, _I, _P, _P, _P, _Z, _P]),
+    "pq_ivf_search": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _I, _P, _P, _I, _I, _P, _P, _P, _P,
+                           _P, _I, _I, _I, _I, _I, _P, _P, _P, _Z, _P]),
     "pq_unpack_rows": (_I, [_P, _L, _L, _I, _I, _I, _P, _P]),
     "pq_unpack_at": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _P]),
     "pq_repack": (_I, [_P, _L, _L, _I, _I, _I, _P, _L, _P]),

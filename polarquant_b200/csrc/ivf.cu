@@ -94,41 +94,76 @@ __global__ void ivf_probe_kernel(const float* __restrict__ qrot, int nq, int d, 
   }
 }
 
-// Gather-ADC over the probed cells.  Block (j*S + s, q) scores slice s of the
-// CSR row list of probe cell j of query q at precision P and keeps its top-K.
+// Grouped gather-ADC (remex/ivf.py:348-374 coarse scoring over the probed
+// cells' rows): block (g, q) scores share g of query q's probe-row list -- the
+// concatenation of its nprobe cells' CSR ranges, split into G equal parts --
+// at precision P and keeps its top-K.  With `cell_rows` (the packed rows and
+// norms copied in CSR order) each probed cell is read as one contiguous run;
+// without it rows are gathered through sorted_idx.  Output ids are corpus rows.
 template <int B, int P>
 __global__ void __launch_bounds__(256)
-ivf_scan_kernel(const uint8_t* __restrict__ packed, int64_t ldb, const float* __restrict__ norms,
-                int d, const float* __restrict__ qrot, const float* __restrict__ cent,
-                const int* __restrict__ probe, int nprobe, int S,
-                const long long* __restrict__ sorted_idx, const long long* __restrict__ offsets,
-                int K, float* __restrict__ out_s, long long* __restrict__ out_id) {
+ivf_group_scan_kernel(const uint8_t* __restrict__ packed, int64_t ldb,
+                      const float* __restrict__ norms, const uint8_t* __restrict__ cell_rows,
+                      const float* __restrict__ cell_norms, int d,
+                      const float* __restrict__ qrot, const float* __restrict__ cent,
+                      const int* __restrict__ probe, int nprobe, int G,
+                      const long long* __restrict__ sorted_idx,
+                      const long long* __restrict__ offsets, int K, float* __restrict__ out_s,
+                      long long* __restrict__ out_id) {
   extern __shared__ __align__(16) char smem[];
-  const int q = blockIdx.y, part = blockIdx.x;
-  const int j = part / S, s = part % S;
+  const int q = blockIdx.y, g = blockIdx.x;
   const size_t st_floats = query_state_floats<P>(d);
   float* st = reinterpret_cast<float*>(smem);
+  long long* pre = reinterpret_cast<long long*>(smem + align_up(st_floats * sizeof(float), 16));
+  long long* cstart = pre + (nprobe + 1);
   build_query_state<P>(qrot + (size_t)q * d, d, cent, st, st, st + d);
+  for (int j = threadIdx.x; j < nprobe; j += blockDim.x) {
+    const int c = probe[(size_t)q * nprobe + j];
+    cstart[j] = offsets[c];
+    pre[j + 1] = offsets[c + 1] - offsets[c];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    pre[0] = 0;
+    for (int j = 0; j < nprobe; ++j) pre[j + 1] += pre[j];
+  }
   BlockTopK tk;
-  tk.init(smem + align_up(st_floats * sizeof(float), 16), K, BlockTopK::cap_for(K, blockDim.x));
-  const int cell = probe[(size_t)q * nprobe + j];
-  const long long a = offsets[cell], b = offsets[cell + 1];
-  const long long len = b - a;
-  const long long lo = a + len * s / S, hi = a + len * (s + 1) / S;
+  tk.init(reinterpret_cast<char*>(cstart + nprobe), K, BlockTopK::cap_for(K, blockDim.x));
+  const long long T = pre[nprobe];
+  const long long lo = T * g / G, hi = T * (g + 1) / G;
   const int lane = threadIdx.x & 31;
+  // Cell of the thread's first element by binary search, then advanced as the
+  // element index grows.
+  int j = 0;
+  {
+    const long long e0 = lo + threadIdx.x;
+    int a = 0, b = nprobe;  // pre[a] <= e0 < pre[b]
+    while (b - a > 1) {
+      const int m = (a + b) >> 1;
+      if (pre[m] <= e0) a = m; else b = m;
+    }
+    j = a;
+  }
   for (long long base = lo; base < hi; base += blockDim.x) {
     const long long e = base + threadIdx.x;
     const bool valid = e < hi;
     float sc = 0.f;
     long long r = -1;
     if (valid) {
-      r = sorted_idx[e];
-      sc = score_row<B, P>(packed + r * ldb, d, st, st, st + d, lane) * __ldg(norms + r);
+      while (e >= pre[j + 1]) ++j;
+      const long long pos = cstart[j] + (e - pre[j]);
+      r = sorted_idx[pos];
+      if (cell_rows) {
+        sc = score_row<B, P>(cell_rows + pos * ldb, d, st, st, st + d, lane) *
+             __ldg(cell_norms + pos);
+      } else {
+        sc = score_row<B, P>(packed + r * ldb, d, st, st, st + d, lane) * __ldg(norms + r);
+      }
     }
     tk.offer(valid, sc, r);
     tk.end_round();
   }
-  const size_t o = ((size_t)q * nprobe * S + part) * K;
+  const size_t o = ((size_t)q * G + g) * K;
   tk.write(out_s + o, out_id + o, 0);
 }
 
@@ -174,7 +209,7 @@ int pq_ivf_probe(const float* qrot, int nq, int d, int n_bits, int mode, const f
 }
 
 size_t pq_ivf_workspace_bytes(int nq, int nprobe, int splits, int candidates) {
-  const size_t c = (size_t)nq * nprobe * splits * candidates;
+  const size_t c = (size_t)nq * splits * candidates;
   return align_up((size_t)nq * nprobe * sizeof(int), 256) + align_up(c * sizeof(float), 256) +
          c * sizeof(long long) + 1024;
 }
@@ -183,8 +218,9 @@ int pq_ivf_search(const uint8_t* packed, int64_t ldb, const float* norms, int64_
                   int bits, int coarse_precision, const float* qrot, int nq,
                   const float* cent_coarse, const float* cent_full, int n_bits, int mode,
                   const float* hyperplanes, const int64_t* sorted_idx, const int64_t* offsets,
-                  int nprobe, int splits, int candidates, int k, int rerank, float* out_scores,
-                  int64_t* out_ids, void* ws, size_t ws_bytes, void* stream) {
+                  const uint8_t* cell_rows, const float* cell_norms, int nprobe, int splits,
+                  int candidates, int k, int rerank, float* out_scores, int64_t* out_ids,
+                  void* ws, size_t ws_bytes, void* stream) {
   int rc = check_corpus(packed, ldb, norms, n, d, bits);
   if (rc) return rc;
   PQ_CHECK_ARG(coarse_precision >= 1 && coarse_precision <= bits,
@@ -199,6 +235,10 @@ int pq_ivf_search(const uint8_t* packed, int64_t ldb, const float* norms, int64_
   PQ_CHECK_ARG(qrot && cent_coarse && sorted_idx && offsets && out_scores && out_ids && ws,
                "null pointer argument");
   PQ_CHECK_ARG(!rerank || cent_full, "null full-precision centroids");
+  PQ_CHECK_ARG((cell_rows == nullptr) == (cell_norms == nullptr),
+               "cell_rows and cell_norms must both be given or both be null");
+  PQ_CHECK_ARG(cell_rows == nullptr || ((uintptr_t)cell_rows & 15) == 0,
+               "cell_rows must be 16-byte aligned");
   const size_t need = pq_ivf_workspace_bytes(nq, nprobe, splits, candidates);
   if (ws_bytes < need)
     return fail(PQ_ERR_WORKSPACE, "pq_ivf_search needs %zu workspace bytes, got %zu", need,
@@ -206,23 +246,28 @@ int pq_ivf_search(const uint8_t* packed, int64_t ldb, const float* norms, int64_
   cudaStream_t st = (cudaStream_t)stream;
   Carve cv(ws, ws_bytes);
   int* probe = cv.take<int>((size_t)nq * nprobe);
-  const size_t c = (size_t)nq * nprobe * splits * candidates;
+  const size_t c = (size_t)nq * splits * candidates;
   float* cs = cv.take<float>(c);
   long long* ci = cv.take<long long>(c);
   rc = pq_ivf_probe(qrot, nq, d, n_bits, mode, hyperplanes, nprobe, probe, nullptr, stream);
   if (rc) return rc;
-  const size_t sm = scan_smem(d, coarse_precision, candidates);
-  dim3 grid(nprobe * splits, nq);
+  // `splits` row groups per query, each a 1/splits share of the query's
+  // probed rows (the prefix sums of the probed cells' sizes live in shared
+  // memory next to the query table).
+  const size_t sm = scan_smem(d, coarse_precision, candidates) +
+                    align_up(((size_t)2 * nprobe + 1) * sizeof(long long), 16);
+  dim3 grid(splits, nq);
   PQ_DISPATCH_BP(bits, coarse_precision, {
-    auto kern = ivf_scan_kernel<B_, P_>;
+    auto kern = ivf_group_scan_kernel<B_, P_>;
     rc = set_smem(kern, sm);
     if (rc) return rc;
-    kern<<<grid, kScanThreads, sm, st>>>(packed, ldb, norms, d, qrot, cent_coarse, probe, nprobe,
-                                         splits, (const long long*)sorted_idx,
+    kern<<<grid, kScanThreads, sm, st>>>(packed, ldb, norms, cell_rows, cell_norms, d, qrot,
+                                         cent_coarse, probe, nprobe, splits,
+                                         (const long long*)sorted_idx,
                                          (const long long*)offsets, candidates, cs, ci);
   });
-  PQ_LAUNCH_CHECK("ivf_scan_kernel");
-  const int parts = nprobe * splits;
+  PQ_LAUNCH_CHECK("ivf_group_scan_kernel");
+  const int parts = splits;
   if (!rerank)  // search_coarse: merged coarse top-k
     return launch_merge(cs, ci, parts, candidates, (long long)parts * candidates, candidates, nq,
                         k, 0, out_scores, (long long*)out_ids, st);

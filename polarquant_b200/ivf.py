@@ -81,6 +81,18 @@ class IVFCoarseIndex:
         self._h_cells = self._h_sorted = self._h_offsets = None
         sizes = counts.max().item() if rows.n else 0
         self._max_cell = int(sizes)
+        # The packed rows and norms copied in CSR order (cell by cell), so the
+        # query path reads each probed cell as one contiguous run instead of
+        # gathering rows through sorted_idx.  Costs one more copy of the
+        # corpus on the device.
+        if rows.n:
+            src = rows.buf[: rows.n * rows.ldb].view(rows.n, rows.ldb)
+            self._cell_rows = torch.zeros(rows.n * rows.ldb + 64, dtype=torch.uint8, device=dev)
+            self._cell_rows[: rows.n * rows.ldb].view(rows.n, rows.ldb).copy_(
+                src.index_select(0, self._sorted))
+            self._cell_norms = rows.norms.index_select(0, self._sorted).contiguous()
+        else:
+            self._cell_rows = self._cell_norms = None
 
     # -- host views (remex/ivf.py:81-89 attributes) ---------------------------
     @property
@@ -155,7 +167,9 @@ class IVFCoarseIndex:
             return (np.full((nq, 0), -1, np.int64), np.zeros((nq, 0), np.float32))
         C = int(min(candidates, TOPK_MAX))
         K = int(min(k, C))
-        splits = int(min(64, max(1, -(-self._max_cell // 8192))))
+        # Row groups per query: about 8k probed rows each (at least one).
+        probed = nprobe * (rows.n / self.n_cells)
+        splits = int(min(64, max(1, round(probed / 8192))))
         pr = q._params(dev)
         ws = workspace(_lib.query("pq_ivf_workspace_bytes", nq, nprobe, splits, C), dev)
         out_s = torch.empty((nq, K), dtype=torch.float32, device=dev)
@@ -163,7 +177,8 @@ class IVFCoarseIndex:
         _lib.call("pq_ivf_search", ptr(rows.buf), rows.ldb, ptr(rows.norms), rows.n, rows.d,
                   rows.bits, precision, ptr(Qr), nq, ptr(pr.cent[precision]),
                   ptr(pr.cent[q.bits]), self.n_bits, 0 if self.mode == "lsh" else 1,
-                  ptr(self._H), ptr(self._sorted), ptr(self._offsets), nprobe, splits, C, K,
+                  ptr(self._H), ptr(self._sorted), ptr(self._offsets), ptr(self._cell_rows),
+                  ptr(self._cell_norms), nprobe, splits, C, K,
                   1 if rerank else 0, ptr(out_s), ptr(out_i), ptr(ws), ws.numel(),
                   stream_ptr(dev))
         return out_i.cpu().numpy(), out_s.cpu().numpy()
