@@ -60,9 +60,13 @@ struct I8Geo {
   static constexpr int RAWBYTES = (B == 8) ? 3 * 16384 : 16384;
   static constexpr int RAW = RAWBYTES / RAWSTAGE;     // ring slots: 4 (2-bit), 2 (4-bit), 3 (8-bit)
   static constexpr int DW = 4;                        // decoder warps
-  static constexpr int SPR = RB / 16;                 // 16-byte raw segments per row per K block
+  // Raw segment per decoder task: 8 bytes for 4-bit codes (16 codes -> one
+  // 16-byte output chunk, so 8 consecutive lanes write one whole 128-byte row
+  // of a plane: conflict-free for any 8-lane phase), else 16 bytes.
+  static constexpr int SEGB = (B == 4) ? 8 : 16;
+  static constexpr int SPR = RB / SEGB;               // raw segments per row per K block
   static constexpr int UPT = kQNh * SPR / (DW * 32);  // segments per decoder thread per stage
-  static constexpr int CPS = 8 / B;                   // 16-code output chunks per segment
+  static constexpr int CPS = SEGB * 8 / B / 16;       // 16-code output chunks per segment
   static_assert(RAW >= 2 && UPT >= 1 && UPT * DW * 32 == kQNh * SPR, "decoder geometry");
 };
 
@@ -118,6 +122,29 @@ __device__ __forceinline__ void byte_lookup(uint32_t w, int shift, uint32_t mask
   l = (prmt(TL[0], TL[1], s) & ~m) | (prmt(TL[2], TL[3], s) & m);
 }
 
+// 16-byte shared-memory load / store at a shared-window address.
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint2 ld_shared_v2(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
 struct PairWalkI8 {
   int t, tile, kb, tiles;
   int64_t r0, r1;
@@ -169,7 +196,6 @@ pair_i8_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant_
   int* scratch_i = reinterpret_cast<int*>(gmeta + 8 * NBAR_MAX + 16 + 1024 + 4 * kBatScratch * 4);
   const uint32_t raw_ring =
       (meta + 8 * NBAR_MAX + 16 + 1024 + 4 * kBatScratch * 8 + 127u) & ~127u;
-  const uint8_t* graw = smem_raw + (raw_ring - raw);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = tc::cluster_ctarank();
@@ -348,7 +374,7 @@ pair_i8_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant_
     }
   } else if (warp >= 10) {
     // ---------------- decoder: this CTA's 128 rows of each stage ----------------
-    // Thread dt owns UPT 16-byte segments u = dt + i * 128 of the stage's raw
+    // Thread dt owns UPT raw segments u = dt + i * 128 of the stage's raw
     // tile (row u / SPR, segment u % SPR) and writes their digits into the
     // swizzled hi/lo planes.  Rows past the chunk decode to finite digits and
     // are ignored by the epilogue.
@@ -376,15 +402,21 @@ pair_i8_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant_
       const uint32_t ph = (uint32_t)(it / S) & 1u;
       if (!tc::mbar_wait(bar(RAWFULL + rr), rph, abort_flag, tc::kErrWaitTmaFull)) break;
       uint32_t cur[G::UPT][4];
-      const uint8_t* rawp = graw + rr * G::RAWSTAGE;
+      const uint32_t rawa = raw_ring + (uint32_t)(rr * G::RAWSTAGE);
 #pragma unroll
       for (int i = 0; i < G::UPT; ++i) {
-        const uint4 v = *reinterpret_cast<const uint4*>(rawp + (dt + i * G::DW * 32) * 16);
-        cur[i][0] = v.x; cur[i][1] = v.y; cur[i][2] = v.z; cur[i][3] = v.w;
+        const uint32_t a = rawa + (uint32_t)(dt + i * G::DW * 32) * (uint32_t)G::SEGB;
+        if constexpr (G::SEGB == 8) {
+          const uint2 v = ld_shared_v2(a);
+          cur[i][0] = v.x; cur[i][1] = v.y; cur[i][2] = 0u; cur[i][3] = 0u;
+        } else {
+          const uint4 v = ld_shared_v4(a);
+          cur[i][0] = v.x; cur[i][1] = v.y; cur[i][2] = v.z; cur[i][3] = v.w;
+        }
       }
       if (!tc::mbar_wait(bar(EMPTY + s), ph ^ 1u, abort_flag, tc::kErrWaitStageEmpty)) break;
-      uint8_t* xh = gbase + (size_t)s * STAGE + 2 * QPLANE;
-      uint8_t* xl = xh + XPLANE;
+      const uint32_t xh = base + (uint32_t)s * STAGE + 2 * QPLANE;
+      const uint32_t xl = xh + XPLANE;
 #pragma unroll
       for (int i = 0; i < G::UPT; ++i) {
         const int u = dt + i * G::DW * 32;
@@ -418,8 +450,8 @@ pair_i8_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant_
           }
           const int c = sg * G::CPS + ch;
           const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(c ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(xh + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-          *reinterpret_cast<uint4*>(xl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+          st_shared_v4(xh + off, hw[0], hw[1], hw[2], hw[3]);
+          st_shared_v4(xl + off, lw[0], lw[1], lw[2], lw[3]);
         }
       }
       // Generic-proxy stores become visible to the tensor core (async proxy);
