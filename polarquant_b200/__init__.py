@@ -12,6 +12,7 @@ from .core import CompressedVectors, PackedVectors, Quantizer
 from .ivf import IVFCoarseIndex
 from .packing import pack, packed_nbytes, unpack
 from .params import lloyd_max_codebook, nested_codebooks
+from .pq_format import load_pq, save_params, save_pq
 
 __version__ = "0.5.0"
 __all__ = [
@@ -20,6 +21,7 @@ __all__ = [
     "IVFCoarseIndex",
     "lloyd_max_codebook", "nested_codebooks",
     "pack", "unpack", "packed_nbytes",
+    "save_pq", "load_pq", "save_params",
 ]
 
 
