@@ -175,8 +175,9 @@ int pq_adc_scan_noalloc(const uint8_t* packed, int64_t ldb, const float* norms, 
  * sum_j q_rot[j]*cent_full[code_j]*norm of those rows, top-k.
  * candidates <= PQ_TOPK_MAX, candidates <= n, k <= candidates.
  * cent_coarse: 2^coarse_precision centroids; cent_full: 2^bits centroids.
- * Batches of >= 64 queries with candidates <= 256 run the coarse stage on the
- * tensor cores (as pq_adc_batch); smaller batches use the streaming scan.
+ * With candidates <= 256, batches of >= 64 queries (>= 8 on corpora of at
+ * least 2^20 rows) run the coarse stage on the tensor cores (as
+ * pq_adc_batch); other batches use the streaming scan.
  * ------------------------------------------------------------------------- */
 size_t pq_twostage_workspace_bytes(int64_t n, int d, int nq, int candidates);
 int pq_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,

@@ -33,6 +33,21 @@ from .params import haar_rotation, lloyd_max_codebook, nested_codebooks
 
 TOPK_MAX = _lib.PQ_TOPK_MAX
 BATCH_MIN = 64       # queries per call from which the tensor-core path is used
+BATCH_MIN_LARGE = 8  # ... on corpora of at least LARGE_ROWS rows
+LARGE_ROWS = 1 << 20
+
+
+def use_tensor_cores(n: int, nq: int, k: int) -> bool:
+    """Whether a batch of nq queries runs the tensor-core ADC (pq_adc_batch).
+
+    The batched kernels process 256 queries per tile whatever the batch size;
+    at d=1536 one pass of them over the corpus costs about as much as 3-4
+    single-query streaming scans, so on large corpora (where their fixed
+    start-up cost is negligible) batches of 8 or more queries are faster on
+    the tensor cores.  pq_twostage applies the same rule to its coarse stage."""
+    if k > BATCH_MAX_K:
+        return False
+    return nq >= BATCH_MIN or (nq >= BATCH_MIN_LARGE and n >= LARGE_ROWS)
 BATCH_MAX_K = 256    # largest k of the tensor-core path
 
 
@@ -495,7 +510,7 @@ class Quantizer:
               force: Optional[str] = None):
         """Top-min(k, n) ADC results for each row of qrot, on the device.
 
-        Batches of BATCH_MIN or more queries (k <= BATCH_MAX_K) run on the
+        Batches chosen by use_tensor_cores() (k <= BATCH_MAX_K) run on the
         tensor cores (pq_adc_batch); smaller ones stream the corpus once per
         query (pq_adc_scan).  `force` ("batch" / "scan") selects a path."""
         dev = rows.device
@@ -505,7 +520,7 @@ class Quantizer:
             return (torch.empty((nq, 0), dtype=torch.float32, device=dev),
                     torch.empty((nq, 0), dtype=torch.int64, device=dev))
         cent = self._params(dev).cent[p]
-        batched = nq >= BATCH_MIN and K <= BATCH_MAX_K if force is None else force == "batch"
+        batched = use_tensor_cores(rows.n, nq, K) if force is None else force == "batch"
         fn = "pq_adc_batch" if batched else "pq_adc_scan"
         ws = workspace(_lib.query(fn + "_workspace_bytes", rows.n, rows.d, nq, K), dev)
         out_s = torch.empty((nq, K), dtype=torch.float32, device=dev)

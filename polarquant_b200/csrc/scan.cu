@@ -373,6 +373,15 @@ int pq_adc_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
 // Query batches at least this large run the coarse stage of two-stage search
 // on the tensor cores (batched ADC); smaller ones use the streaming scan.
 constexpr int kTwostageBatchMin = 64;
+// ... and on corpora of at least kTwostageLargeRows rows from this many: one
+// pass of the batched kernels costs a few single-query scans there.
+constexpr int kTwostageBatchMinLarge = 8;
+constexpr int64_t kTwostageLargeRows = 1 << 20;
+
+static bool twostage_batched(int64_t n, int nq, int candidates) {
+  return candidates <= 256 &&
+         (nq >= kTwostageBatchMin || (nq >= kTwostageBatchMinLarge && n >= kTwostageLargeRows));
+}
 
 static size_t batched_ws(int64_t n, int d, int nq, int k);
 
@@ -384,7 +393,7 @@ static size_t twostage_exact_offset(int64_t n, int d, int nq, int candidates) {
 
 size_t pq_twostage_workspace_bytes(int64_t n, int d, int nq, int candidates) {
   const size_t a = pq_adc_scan_workspace_bytes(n, d, nq, candidates);
-  if (nq >= kTwostageBatchMin && candidates <= 256) {
+  if (twostage_batched(n, nq, candidates)) {
     const size_t b = twostage_exact_offset(n, d, nq, candidates) +
                      align_up((size_t)nq * candidates * sizeof(float), 256) +
                      (size_t)nq * candidates * sizeof(long long) + 256;
@@ -442,7 +451,7 @@ int pq_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
   float* cs;
   long long* ci;
   int nblk;
-  if (nq >= kTwostageBatchMin && candidates <= 256) {
+  if (twostage_batched(n, nq, candidates)) {
     int kpart = candidates;
     rc = run_batched(packed, ldb, norms, n, d, bits, coarse_precision, qrot, nq, cent_coarse,
                      candidates, 0, ws, ws_bytes, st, &cs, &ci, &nblk, &kpart);

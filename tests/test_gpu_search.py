@@ -343,3 +343,23 @@ def test_batched_adc_repeatable(gpu, bits, d, k):
         bad = sum(not O.topk_equal_up_to_ties(GI[q], GS[q], SI[q], SS[q], rtol=RTOL)
                   for q in range(len(qs)))
         assert bad == 0, (rep, bad)
+
+
+def test_small_batch_on_large_corpus_uses_tensor_cores(gpu):
+    """16 queries on a corpus of 2^20+ rows take the tensor-core path by
+    default (one batched pass costs a few single-query scans there) and match
+    the oracle's search_adc per query."""
+    from polarquant_b200 import Quantizer
+    from polarquant_b200.core import use_tensor_cores
+    d, n, nq, k = 64, (1 << 20) + 123, 16, 20
+    rng = np.random.default_rng(11)
+    X = unit_rows(rng, n, d)
+    qs = unit_rows(rng, nq, d)
+    pq = Quantizer(d, bits=4, seed=42)
+    cv = pq.encode(X)
+    assert use_tensor_cores(n, nq, k) and not use_tensor_cores(100_000, nq, k)
+    GI, GS = pq.search_adc_many(cv, qs, k=k)
+    idx, norms = cv.indices, cv.norms
+    for q in range(nq):
+        ri, rs = O.search_adc(pq.R, pq.centroids, pq._nested, 4, idx, norms, qs[q], k=k)
+        assert O.topk_equal_up_to_ties(GI[q], GS[q], ri, rs, rtol=RTOL), q
