@@ -483,6 +483,7 @@ pair_i8_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant_
     float* ss = scratch_s + quad * kBatScratch;  // shared by the two halves, used in turn
     int* si = scratch_i + quad * kBatScratch;
     const float csc = p.cscale[0];
+    const int mch = (int)p.cscale[1], mcl = (int)p.cscale[2];
     auto buf_of = [&](int ql) { return (((size_t)blockIdx.x * kQM + ql) * 2 + half) * p.cap; };
     int tcount = 0;
     bool ok = true;
@@ -495,6 +496,9 @@ pair_i8_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant_
       const int qg = qbase + q_lane;
       const bool qv = qg < p.nq;
       const float qs = qv ? p.qinv[qg] * csc : 0.f;
+      // v = HH + round(X / 256) <= HH + xb: |X| <= sum|q_hi| max|c_lo| +
+      // sum|q_lo| max|c_hi|, so a group is bounded by its HH values alone.
+      const int xb = qv ? (p.qdig[2 * qg] * mcl + p.qdig[2 * qg + 1] * mch + 128) >> 8 : 0;
       float* bs = p.buf_s + buf_of(q_lane);
       int* bi = p.buf_i + buf_of(q_lane);
       int cnt = 0;
@@ -539,15 +543,15 @@ pair_i8_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant_
         if (gkey != 0u) thr = fmaxf(thr, key_to_float(gkey));
         const uint32_t taddr =
             tmem_base + ((uint32_t)(32 * quad) << 16) + (uint32_t)(half * (kQN / 2));
-        // 16-column groups g = 0..7 of the half.
+        // 16-column groups g = 0..7 of the half: the HH accumulator decides
+        // whether a group can hold a candidate; the cross terms are read only
+        // for groups that can.
 #pragma unroll 1
         for (int g = 0; g < 8; ++g) {
-          uint32_t h[16], x[16];
+          uint32_t h[16];
           __syncwarp();
           tc::tmem_ld16(taddr + (uint32_t)(16 * g), h);
-          tc::tmem_ld16(taddr + (uint32_t)(kQN + 16 * g), x);
           tc::tmem_ld_wait(h);
-          tc::tmem_ld_wait(x);
           if ((g & 1) == 0) {
             // Room for 32 more candidates in every buffer of the warp.
             uint32_t need = __ballot_sync(0xffffffffu, qv && cnt + 32 > p.cap);
@@ -571,19 +575,20 @@ pair_i8_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant_
           const float gmin = __shfl_sync(
               0xffffffffu, c == 0 ? nmn[0] : c == 1 ? nmn[1] : c == 2 ? nmn[2] : nmn[3],
               16 * (g & 1));
-          int t8[8];                                   // tree max of the 16 combined values
+          int t8[8];                                   // tree max of the 16 HH values
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            t8[i] = max((int)h[i] + (((int)x[i] + 128) >> 8),
-                        (int)h[i + 8] + (((int)x[i + 8] + 128) >> 8));
+          for (int i = 0; i < 8; ++i) t8[i] = max((int)h[i], (int)h[i + 8]);
 #pragma unroll
           for (int i = 0; i < 4; ++i) t8[i] = max(t8[i], t8[i + 4]);
-          const int vmax = max(max(t8[0], t8[2]), max(t8[1], t8[3]));
+          const int vmax = max(max(t8[0], t8[2]), max(t8[1], t8[3])) + xb;
           const float bound = (__int2float_rn(vmax) * qs) * (vmax >= 0 ? gmax : gmin);
           const bool want = qv && bound > thr;
           if (__any_sync(0xffffffffu, want)) {
-            // Every row of the group scored; passing rows appended with
-            // predicated stores (no per-row branch).
+            // Every row of the group scored exactly; passing rows appended
+            // with predicated stores (no per-row branch).
+            uint32_t x[16];
+            tc::tmem_ld16(taddr + (uint32_t)(kQN + 16 * g), x);
+            tc::tmem_ld_wait(x);
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const float nr = __shfl_sync(0xffffffffu, nr_all, 16 * (g & 1) + i);
@@ -638,11 +643,14 @@ pair_i8_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant_
 }
 
 // Rotated queries -> 16-bit fixed point split into two int8 planes (rows of
-// ldk bytes, zero past d), one warp per query; qscale[q] = max|q| / 32639.
-// swap != 0 stores coordinate j at position j ^ 1 (the 4-bit decoder's order).
+// ldk bytes, zero past d), one warp per query; qscale[q] = max|q| / 32639 and
+// qdig[2q], qdig[2q+1] = the sums of |hi| and |lo| digits (for the epilogue's
+// bound on the cross-term accumulator).  swap != 0 stores coordinate j at
+// position j ^ 1 (the 4-bit decoder's order).
 __global__ void __launch_bounds__(256)
 qsplit_i8_kernel(const float* __restrict__ qrot, int nq, int d, int ldk, int swap,
-                 int8_t* __restrict__ qhi, int8_t* __restrict__ qlo, float* __restrict__ qscale) {
+                 int8_t* __restrict__ qhi, int8_t* __restrict__ qlo, float* __restrict__ qscale,
+                 int* __restrict__ qdig) {
   const int lane = threadIdx.x & 31;
   const int warps = gridDim.x * (blockDim.x >> 5);
   for (int q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); q < nq; q += warps) {
@@ -654,6 +662,7 @@ qsplit_i8_kernel(const float* __restrict__ qrot, int nq, int d, int ldk, int swa
     const float inv = mx > 0.f ? (float)kQDigitMax / mx : 0.f;
     uint32_t* hp = reinterpret_cast<uint32_t*>(qhi + (size_t)q * ldk);
     uint32_t* lp = reinterpret_cast<uint32_t*>(qlo + (size_t)q * ldk);
+    int shi = 0, slo = 0;
     for (int p0 = 4 * lane; p0 < ldk; p0 += 128) {
       uint32_t hw = 0, lw = 0;
 #pragma unroll
@@ -664,13 +673,21 @@ qsplit_i8_kernel(const float* __restrict__ qrot, int nq, int d, int ldk, int swa
         qi = max(-kQDigitMax, min(kQDigitMax, qi));
         const int hi = (qi + 128) >> 8;
         const int lo = qi - (hi << 8);
+        shi += abs(hi);
+        slo += abs(lo);
         hw |= (uint32_t)(hi & 255) << (8 * t);
         lw |= (uint32_t)(lo & 255) << (8 * t);
       }
       hp[p0 >> 2] = hw;
       lp[p0 >> 2] = lw;
     }
-    if (lane == 0) qscale[q] = mx > 0.f ? mx / (float)kQDigitMax : 0.f;
+    shi = (int)__reduce_add_sync(0xffffffffu, (unsigned)shi);
+    slo = (int)__reduce_add_sync(0xffffffffu, (unsigned)slo);
+    if (lane == 0) {
+      qscale[q] = mx > 0.f ? mx / (float)kQDigitMax : 0.f;
+      qdig[2 * q] = shi;
+      qdig[2 * q + 1] = slo;
+    }
   }
 }
 
@@ -679,7 +696,8 @@ qsplit_i8_kernel(const float* __restrict__ qrot, int nq, int d, int ldk, int swa
 // (hi bytes, then lo bytes) of 16 entries c -> cent[c >> reg_shift] (0 past
 // the table): reg_shift = bits - P for 4-bit codes (indexed by the stored
 // code), 0 for 8-bit codes (indexed by the shifted code);
-// cscale[0] = max|cent| / 32639 * 65536.
+// cscale[0] = max|cent| / 32639 * 65536, cscale[1] / [2] = the largest |hi| /
+// |lo| digit.
 __global__ void lut_i8_kernel(const float* __restrict__ cent, int size, int reg_shift,
                               uint32_t* __restrict__ lut, float* __restrict__ cscale) {
   __shared__ float mx;
@@ -709,7 +727,16 @@ __global__ void lut_i8_kernel(const float* __restrict__ cent, int size, int reg_
     }
     lut[256 + threadIdx.x] = v;
   }
-  if (threadIdx.x == 0) cscale[0] = mx / (float)kQDigitMax * 65536.f;
+  if (threadIdx.x == 0) {
+    cscale[0] = mx / (float)kQDigitMax * 65536.f;
+    int mh = 0, ml = 0;  // largest |hi| and |lo| digit of the table
+    for (int i = 0; i < size; ++i) {
+      mh = max(mh, abs((int)(int8_t)(ent[i] & 255u)));
+      ml = max(ml, abs((int)(int8_t)((ent[i] >> 8) & 255u)));
+    }
+    cscale[1] = (float)mh;
+    cscale[2] = (float)ml;
+  }
 }
 
 struct I8Plan {
@@ -828,6 +855,7 @@ struct I8Ws {
   float *qscale, *cscale, *buf_s, *out_s;
   uint32_t* lut;
   unsigned int* gthr;
+  int* qdig;
   int* buf_i;
   long long* out_id;
 };
@@ -840,6 +868,7 @@ static size_t i8_ws_carve(const I8Plan& b, int nq, int K, void* ws, size_t ws_by
   w->cscale = cv.take<float>(4);
   w->lut = cv.take<uint32_t>(256 + 8);
   w->gthr = cv.take<unsigned int>((size_t)b.nq_pad);
+  w->qdig = cv.take<int>((size_t)2 * b.nq_pad);
   w->buf_s = cv.take<float>((size_t)b.grid * kQM * 2 * b.cap);
   w->buf_i = cv.take<int>((size_t)b.grid * kQM * 2 * b.cap);
   w->out_s = cv.take<float>((size_t)nq * 2 * b.rchunks * K);
@@ -887,7 +916,7 @@ static int run_batched_i8(const uint8_t* packed, int64_t ldb, const float* norms
   {
     const int pg = (nq + 7) / 8 < num_sms() * 16 ? (nq + 7) / 8 : num_sms() * 16;
     qsplit_i8_kernel<<<pg, 256, 0, st>>>(qrot, nq, d, b.ldk, bits == 4 ? 1 : 0, w.qhi, w.qlo,
-                                         w.qscale);
+                                         w.qscale, w.qdig);
     PQ_LAUNCH_CHECK("qsplit_i8_kernel");
   }
   const int lut_size = 1 << precision;
@@ -905,6 +934,7 @@ static int run_batched_i8(const uint8_t* packed, int64_t ldb, const float* norms
   a.rows_per_chunk = b.rpc; a.K = K; a.cap = b.cap; a.qinv = w.qscale; a.cscale = w.cscale;
   a.lut = w.lut; a.lut_size = lut_size; a.buf_s = w.buf_s; a.buf_i = w.buf_i;
   a.out_s = w.out_s; a.out_id = w.out_id; a.row_offset = row_offset; a.gthr = w.gthr;
+  a.qdig = w.qdig;
   cudaLaunchConfig_t cfg;
   cudaLaunchAttribute at[1];
   i8_config(&cfg, at, b.grid, b.smem, st);
