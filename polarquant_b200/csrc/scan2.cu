@@ -83,6 +83,103 @@ __host__ __device__ __forceinline__ int s2_tab_index(int j, int c, int cpr) {
   return ((j % cpr) >= cpr / 2) ? (t ^ 16) : t;
 }
 
+// The query's table in shared memory (all threads of the block).  Table mode
+// (P <= 4): T[j][c] = fl(q_rot[j] * cent[c]) at s2_tab_index(j, c).  Direct
+// mode: cent[c] replicated per lane, then q_rot per slab as
+// [first half][4 pad][second half][4 pad] (CPR + 8 floats), so the two
+// half-warps' broadcast reads fall in different banks.
+template <int B, int P>
+__device__ __forceinline__ void s2_fill_table(float* gtab, const float* __restrict__ qv,
+                                              const float* __restrict__ cent, int d, int slabs) {
+  constexpr int CPR = kS2Slab * 8 / B;
+  const int jmax = slabs * CPR;
+  if constexpr (P <= 4) {
+    for (int i = threadIdx.x; i < jmax * 16; i += blockDim.x) {
+      const int j = i >> 4, c = i & 15;
+      gtab[s2_tab_index(j, c, CPR)] =
+          (j < d && c < (1 << P)) ? __fmul_rn(__ldg(qv + j), __ldg(cent + c)) : 0.f;
+    }
+  } else {
+    for (int i = threadIdx.x; i < (1 << P) * 32; i += blockDim.x) gtab[i] = __ldg(cent + (i >> 5));
+    float* Q = gtab + (1 << P) * 32;
+    for (int i = threadIdx.x; i < jmax; i += blockDim.x) {
+      const int sl = i / CPR, jl = i % CPR;
+      Q[sl * (CPR + 8) + jl + ((jl >= CPR / 2) ? 4 : 0)] = (i < d) ? __ldg(qv + i) : 0.f;
+    }
+  }
+}
+
+// Adds the row's partial sums over one 128-byte slab (two threads per row:
+// half h of the slab) to a0..a3.  buf: shared address of the row's slab in the
+// stage; tab: the query table; the rest as in scan2_kernel.
+template <int B, int P>
+__device__ __forceinline__ void s2_slab(uint32_t buf, uint32_t swz, uint32_t tab, int slab, int h,
+                                        int lane, float& a0, float& a1, float& a2, float& a3) {
+  constexpr bool TABLE = P <= 4;
+  constexpr int CPR = kS2Slab * 8 / B;
+  const uint32_t pos_hi = h ? 0xC040C040u : 0x80008000u;
+  const uint32_t pos_lo = h ? 0x80008000u : 0xC040C040u;
+  const uint32_t pos_b = h ? 0x80C00040u : 0xC0804000u;
+  if constexpr (TABLE) {
+    // 256-aligned base of this half's table pages
+    const uint32_t tbs = tab + (uint32_t)(slab * CPR) * 64u + (uint32_t)h * (CPR / 2) * 64u;
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      const uint32_t c = (uint32_t)(4 * h + cc);
+      const uint4 v = lds_u128(buf + ((c ^ swz) << 4));
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if constexpr (B == 4) {
+          const uint32_t oh = code_offsets<4, P, true>(w[i], pos_hi);
+          const uint32_t ol = code_offsets<4, P, false>(w[i], pos_lo);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t pg = 256u * (uint32_t)(8 * cc + 2 * i + (k >> 1));
+            const uint32_t sel = 0x7650u | (uint32_t)k;
+            const float th = lds_f32(__byte_perm(oh, tbs, sel) + pg);
+            const float tl = lds_f32(__byte_perm(ol, tbs, sel) + pg);
+            if (k & 1) { a1 += th; a3 += tl; } else { a0 += th; a2 += tl; }
+          }
+        } else {
+          const uint32_t o = code_offsets<8, P, true>(w[i], pos_b);
+          const uint32_t pg = 256u * (uint32_t)(4 * cc + i);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float t = lds_f32(__byte_perm(o, tbs, 0x7650u | (uint32_t)k) + pg);
+            if (k == 0) a0 += t; else if (k == 1) a1 += t; else if (k == 2) a2 += t; else a3 += t;
+          }
+        }
+      }
+    }
+  } else {
+    const uint32_t cb = tab + (uint32_t)lane * 4u;
+    const uint32_t qb = tab + (uint32_t)(1 << P) * 128u +
+                        (uint32_t)(slab * (CPR + 8) + h * (CPR / 2 + 4)) * 4u;
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      const uint32_t c = (uint32_t)(4 * h + cc);
+      const uint4 v = lds_u128(buf + ((c ^ swz) << 4));
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 qq = lds_u128(qb + (uint32_t)(16 * cc + 4 * i) * 4u);
+        const float qf[4] = {__uint_as_float(qq.x), __uint_as_float(qq.y),
+                             __uint_as_float(qq.z), __uint_as_float(qq.w)};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t code = (w[i] >> (8 * k + 8 - P)) & ((1u << P) - 1u);
+          const float cv = lds_f32(cb + code * 128u);
+          if (k == 0) a0 = fmaf(qf[k], cv, a0);
+          else if (k == 1) a1 = fmaf(qf[k], cv, a1);
+          else if (k == 2) a2 = fmaf(qf[k], cv, a2);
+          else a3 = fmaf(qf[k], cv, a3);
+        }
+      }
+    }
+  }
+}
+
 template <int B, int P>
 __global__ void __launch_bounds__(kS2Threads, 1)
 scan2_kernel(const __grid_constant__ CUtensorMap tmap, const float* __restrict__ norms,
@@ -90,8 +187,6 @@ scan2_kernel(const __grid_constant__ CUtensorMap tmap, const float* __restrict__
              int K, int64_t rows_per_block, int nblk, int slabs, int stages, int lut_bytes,
              float* __restrict__ cand_s, long long* __restrict__ cand_id) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  constexpr bool TABLE = P <= 4;
-  constexpr int CPR = kS2Slab * 8 / B;  // codes per slab row
   constexpr uint32_t STAGE = kS2Rows * kS2Slab;
   const uint32_t raw = tc::smem_u32(smem_raw);
   // [slab buffers, 1024-aligned][table][8 x 8-byte barriers][top-k buffer]
@@ -104,23 +199,7 @@ scan2_kernel(const __grid_constant__ CUtensorMap tmap, const float* __restrict__
   const int q = blockIdx.y, b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31;
   const float* qv = qrot + (size_t)q * d;
-  const int jmax = slabs * CPR;
-  if constexpr (TABLE) {
-    for (int i = tid; i < jmax * 16; i += kS2Threads) {
-      const int j = i >> 4, c = i & 15;
-      gtab[s2_tab_index(j, c, CPR)] =
-          (j < d && c < (1 << P)) ? __fmul_rn(__ldg(qv + j), __ldg(cent + c)) : 0.f;
-    }
-  } else {
-    for (int i = tid; i < (1 << P) * 32; i += kS2Threads) gtab[i] = __ldg(cent + (i >> 5));
-    // q_rot per slab: [first half][4 pad][second half][4 pad] (CPR + 8 floats),
-    // so the two half-warps' broadcast reads fall in different banks.
-    float* Q = gtab + (1 << P) * 32;
-    for (int i = tid; i < jmax; i += kS2Threads) {
-      const int sl = i / CPR, jl = i % CPR;
-      Q[sl * (CPR + 8) + jl + ((jl >= CPR / 2) ? 4 : 0)] = (i < d) ? __ldg(qv + i) : 0.f;
-    }
-  }
+  s2_fill_table<B, P>(gtab, qv, cent, d, slabs);
   if (tid == 0) {
     for (int s = 0; s < stages; ++s) tc::mbar_init(bars + 8u * s, 1);
     *abort_flag = 0;
@@ -150,10 +229,6 @@ scan2_kernel(const __grid_constant__ CUtensorMap tmap, const float* __restrict__
   const int rt = (tid >> 5) * 16 + (lane & 15);  // row within the tile
   const uint32_t swz = (uint32_t)(rt & 7);
   const uint32_t rowoff = (uint32_t)rt * kS2Slab;
-  // Page positions (see s2_tab_index): 4-bit high / low nibbles, 8-bit bytes.
-  const uint32_t pos_hi = h ? 0xC040C040u : 0x80008000u;
-  const uint32_t pos_lo = h ? 0x80008000u : 0xC040C040u;
-  const uint32_t pos_b = h ? 0x80C00040u : 0xC0804000u;
   float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
   bool ok = true;
   int slab = 0;
@@ -165,65 +240,8 @@ scan2_kernel(const __grid_constant__ CUtensorMap tmap, const float* __restrict__
       if (ok && tid == 0) confirmed = it + 1;
     }
     if (ok) {
-      const uint32_t buf = sbase + (uint32_t)s * STAGE + rowoff;
-      if constexpr (TABLE) {
-        // 256-aligned base of this half's table pages
-        const uint32_t tbs = tab + (uint32_t)(slab * CPR) * 64u + (uint32_t)h * (CPR / 2) * 64u;
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const uint32_t c = (uint32_t)(4 * h + cc);
-          const uint4 v = lds_u128(buf + ((c ^ swz) << 4));
-          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            if constexpr (B == 4) {
-              const uint32_t oh = code_offsets<4, P, true>(w[i], pos_hi);
-              const uint32_t ol = code_offsets<4, P, false>(w[i], pos_lo);
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const uint32_t pg = 256u * (uint32_t)(8 * cc + 2 * i + (k >> 1));
-                const uint32_t sel = 0x7650u | (uint32_t)k;
-                const float th = lds_f32(__byte_perm(oh, tbs, sel) + pg);
-                const float tl = lds_f32(__byte_perm(ol, tbs, sel) + pg);
-                if (k & 1) { a1 += th; a3 += tl; } else { a0 += th; a2 += tl; }
-              }
-            } else {
-              const uint32_t o = code_offsets<8, P, true>(w[i], pos_b);
-              const uint32_t pg = 256u * (uint32_t)(4 * cc + i);
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const float t = lds_f32(__byte_perm(o, tbs, 0x7650u | (uint32_t)k) + pg);
-                if (k == 0) a0 += t; else if (k == 1) a1 += t; else if (k == 2) a2 += t; else a3 += t;
-              }
-            }
-          }
-        }
-      } else {
-        const uint32_t cb = tab + (uint32_t)lane * 4u;
-        const uint32_t qb = tab + (uint32_t)(1 << P) * 128u +
-                            (uint32_t)(slab * (CPR + 8) + h * (CPR / 2 + 4)) * 4u;
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const uint32_t c = (uint32_t)(4 * h + cc);
-          const uint4 v = lds_u128(buf + ((c ^ swz) << 4));
-          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint4 qq = lds_u128(qb + (uint32_t)(16 * cc + 4 * i) * 4u);
-            const float qf[4] = {__uint_as_float(qq.x), __uint_as_float(qq.y),
-                                 __uint_as_float(qq.z), __uint_as_float(qq.w)};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint32_t code = (w[i] >> (8 * k + 8 - P)) & ((1u << P) - 1u);
-              const float cv = lds_f32(cb + code * 128u);
-              if (k == 0) a0 = fmaf(qf[k], cv, a0);
-              else if (k == 1) a1 = fmaf(qf[k], cv, a1);
-              else if (k == 2) a2 = fmaf(qf[k], cv, a2);
-              else a3 = fmaf(qf[k], cv, a3);
-            }
-          }
-        }
-      }
+      s2_slab<B, P>(sbase + (uint32_t)s * STAGE + rowoff, swz, tab, slab, h, lane, a0, a1, a2,
+                    a3);
     }
     __syncthreads();  // every thread is done with stage s
     if (tid == 0 && ok && issued < total) {
@@ -256,6 +274,7 @@ scan2_kernel(const __grid_constant__ CUtensorMap tmap, const float* __restrict__
   const size_t o = ((size_t)q * nblk + b) * K;
   tk.write(cand_s + o, cand_id + o, 0);
 }
+
 
 }  // namespace pqb
 
@@ -357,6 +376,8 @@ static int try_scan2(const uint8_t* packed, int64_t ldb, const float* norms, int
   *used = true;
   return PQ_OK;
 }
+
+
 
 extern "C" int pq_adc_scan_kernel(int64_t n, int d, int bits, int precision, int nq, int k,
                                   int64_t ldb) {
