@@ -85,7 +85,7 @@ CHUNK = 65536
 # queries (profiles/pair_i8_kernel_c4s.md: 25.2 GB read + 2.1 GB written),
 # scaled to other row counts of the same workload by rows (traffic grows with
 # the row tiles at a fixed query batch).
-PROFILED_TRAFFIC = {"rows": 4_000_000, "bytes": 27.29e9, "queries": 10_000, "d": 1536,
+PROFILED_TRAFFIC = {"rows": 4_000_000, "bytes": 20.52e9, "queries": 10_000, "d": 1536,
                     "source": "profiles/pair_i8_kernel_c4s.md (4M-row capture, scaled by rows)"}
 
 
