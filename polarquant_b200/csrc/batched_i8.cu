@@ -517,16 +517,15 @@ pair_i8_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant_
           nrm[c] = (ok && row < r1) ? __ldg(p.norms + row) : 0.f;
         }
         const unsigned gkey = (ok && qv) ? __ldcg(p.gthr + qg) : 0u;
-        // Norm range of each 16-row group, also before the wait: after the
-        // reduction lanes 0-15 of register c hold group 2c's, lanes 16-31
-        // group 2c+1's.
+        // Norm range of each 8-row group, also before the wait: after the
+        // reduction lanes 8j..8j+7 of register c hold group 4c+j's.
         float nmx[4], nmn[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           nmx[c] = nrm[c];
           nmn[c] = nrm[c];
 #pragma unroll
-          for (int o = 8; o > 0; o >>= 1) {
+          for (int o = 4; o > 0; o >>= 1) {
             nmx[c] = fmaxf(nmx[c], __shfl_xor_sync(0xffffffffu, nmx[c], o));
             nmn[c] = fminf(nmn[c], __shfl_xor_sync(0xffffffffu, nmn[c], o));
           }
@@ -543,57 +542,67 @@ pair_i8_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant_
         if (gkey != 0u) thr = fmaxf(thr, key_to_float(gkey));
         const uint32_t taddr =
             tmem_base + ((uint32_t)(32 * quad) << 16) + (uint32_t)(half * (kQN / 2));
-        // 16-column groups g = 0..7 of the half: the HH accumulator decides
-        // whether a group can hold a candidate; the cross terms are read only
-        // for groups that can.
-#pragma unroll 1
-        for (int g = 0; g < 8; ++g) {
-          uint32_t h[16];
-          __syncwarp();
-          tc::tmem_ld16(taddr + (uint32_t)(16 * g), h);
-          tc::tmem_ld_wait(h);
-          if ((g & 1) == 0) {
-            // Room for 32 more candidates in every buffer of the warp.
-            uint32_t need = __ballot_sync(0xffffffffu, qv && cnt + 32 > p.cap);
-            while (need) {
-              const int src = __ffs(need) - 1;
-              need &= need - 1;
-              const float before = thr;
-              warp_select(src, lane, cnt, p.buf_s + buf_of(32 * quad + src),
-                          p.buf_i + buf_of(32 * quad + src), p.K, cnt, thr);
-              if (lane == src) {
-                thr = fmaxf(thr, before);  // never below a threshold already adopted
-                atomicMax(p.gthr + qg, ordered_key(thr));  // publish
-              }
+        // The half's 128 columns in four 32-column chunks, 8-row groups of a
+        // chunk: one TMEM load of the chunk's HH values (load latency, not
+        // arithmetic, bounds this loop), then per group two bounds of its
+        // scores -- HH + xb (loose by the worst case of the cross terms) and,
+        // for groups that pass it, the group's largest v after loading its
+        // cross terms -- and only the rows of groups that pass both are
+        // scored.  float(v) * qs * norm is monotonic in v and in the norm
+        // (IEEE rounding is), so both are upper bounds of every score of the
+        // group.
+        auto room = [&]() {
+          // Room for 32 more candidates in every buffer of the warp.
+          uint32_t need = __ballot_sync(0xffffffffu, qv && cnt + 32 > p.cap);
+          while (need) {
+            const int src = __ffs(need) - 1;
+            need &= need - 1;
+            const float before = thr;
+            warp_select(src, lane, cnt, p.buf_s + buf_of(32 * quad + src),
+                        p.buf_i + buf_of(32 * quad + src), p.K, cnt, thr);
+            if (lane == src) {
+              thr = fmaxf(thr, before);  // never below a threshold already adopted
+              atomicMax(p.gthr + qg, ordered_key(thr));  // publish
             }
           }
-          const int c = g >> 1;                       // rows of groups 2c, 2c + 1
+        };
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          room();
+          uint32_t h[32];
+          __syncwarp();
+          tc::tmem_ld32(taddr + (uint32_t)(32 * c), h);
+          tc::tmem_ld_wait(h);
           const float nr_all = c == 0 ? nrm[0] : c == 1 ? nrm[1] : c == 2 ? nrm[2] : nrm[3];
-          const float gmax = __shfl_sync(
-              0xffffffffu, c == 0 ? nmx[0] : c == 1 ? nmx[1] : c == 2 ? nmx[2] : nmx[3],
-              16 * (g & 1));
-          const float gmin = __shfl_sync(
-              0xffffffffu, c == 0 ? nmn[0] : c == 1 ? nmn[1] : c == 2 ? nmn[2] : nmn[3],
-              16 * (g & 1));
-          int t8[8];                                   // tree max of the 16 HH values
+          const float nmx_c = c == 0 ? nmx[0] : c == 1 ? nmx[1] : c == 2 ? nmx[2] : nmx[3];
+          const float nmn_c = c == 0 ? nmn[0] : c == 1 ? nmn[1] : c == 2 ? nmn[2] : nmn[3];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) t8[i] = max((int)h[i], (int)h[i + 8]);
+          for (int j = 0; j < 4; ++j) {
+            const float gmax = __shfl_sync(0xffffffffu, nmx_c, 8 * j);
+            const float gmin = __shfl_sync(0xffffffffu, nmn_c, 8 * j);
+            int t4[4];                                 // tree max of the group's 8 HH values
 #pragma unroll
-          for (int i = 0; i < 4; ++i) t8[i] = max(t8[i], t8[i + 4]);
-          const int vmax = max(max(t8[0], t8[2]), max(t8[1], t8[3])) + xb;
-          const float bound = (__int2float_rn(vmax) * qs) * (vmax >= 0 ? gmax : gmin);
-          const bool want = qv && bound > thr;
-          if (__any_sync(0xffffffffu, want)) {
+            for (int i = 0; i < 4; ++i) t4[i] = max((int)h[8 * j + i], (int)h[8 * j + i + 4]);
+            const int hmax = max(max(t4[0], t4[2]), max(t4[1], t4[3])) + xb;
+            bool want = qv && (__int2float_rn(hmax) * qs) * (hmax >= 0 ? gmax : gmin) > thr;
+            if (!__any_sync(0xffffffffu, want)) continue;
+            uint32_t x[8];
+            __syncwarp();
+            tc::tmem_ld8(taddr + (uint32_t)(kQN + 32 * c + 8 * j), x);
+            tc::tmem_ld_wait(x);
+            int vmax = (int)h[8 * j] + (((int)x[0] + 128) >> 8);
+#pragma unroll
+            for (int i = 1; i < 8; ++i)
+              vmax = max(vmax, (int)h[8 * j + i] + (((int)x[i] + 128) >> 8));
+            want = want && (__int2float_rn(vmax) * qs) * (vmax >= 0 ? gmax : gmin) > thr;
+            if (!__any_sync(0xffffffffu, want)) continue;
             // Every row of the group scored exactly; passing rows appended
             // with predicated stores (no per-row branch).
-            uint32_t x[16];
-            tc::tmem_ld16(taddr + (uint32_t)(kQN + 16 * g), x);
-            tc::tmem_ld_wait(x);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float nr = __shfl_sync(0xffffffffu, nr_all, 16 * (g & 1) + i);
-              const int64_t row = hr0 + 16 * g + i;
-              const int v = (int)h[i] + (((int)x[i] + 128) >> 8);
+            for (int i = 0; i < 8; ++i) {
+              const float nr = __shfl_sync(0xffffffffu, nr_all, 8 * j + i);
+              const int64_t row = hr0 + 32 * c + 8 * j + i;
+              const int v = (int)h[8 * j + i] + (((int)x[i] + 128) >> 8);
               const float sc = (__int2float_rn(v) * qs) * nr;
               const bool pass = want && row < r1 && sc > thr;
               if (pass) {
