@@ -8,7 +8,8 @@ tests restate that arithmetic on the host and check the two facts the design
 relies on: the approximate scores stay within a small absolute band of the
 exact ones, and every row of the exact top K is among the approximate top
 K+32 (so the exact rescoring recovers the exact top K).  They also check the
-epilogue's group bound v <= HH + xb.
+epilogue's two bounds of an 8-row group (HH + xb, then the group's largest v)
+in its f32 arithmetic.
 """
 
 import numpy as np
@@ -79,3 +80,41 @@ def test_exact_topk_within_int8_candidates(d, bits, prec, clusters):
         top = np.argsort(-exact[q], kind="stable")[:k]
         cand = set(np.argsort(-approx[q], kind="stable")[:k + MARGIN].tolist())
         assert set(top.tolist()) <= cand, q
+
+
+def test_group_bounds_cover_every_score():
+    """The epilogue's two bounds of an 8-row group, in the kernel's f32
+    arithmetic: float(max HH + xb) * qs * (max or min norm) and
+    float(max v) * qs * (max or min norm) are >= every row's
+    float(v) * qs * norm, and the second is never looser than the first."""
+    rng = np.random.default_rng(7)
+    d, bits, n, nq = 512, 4, 4096, 8
+    X = rng.standard_normal((n, d)).astype(np.float32)
+    X /= np.linalg.norm(X, axis=1, keepdims=True)
+    norms_all = np.exp(rng.uniform(np.log(0.5), np.log(2.0), n)).astype(np.float32)
+    Q = rng.standard_normal((nq, d)).astype(np.float32)
+    Q /= np.linalg.norm(Q, axis=1, keepdims=True)
+    R = haar_rotation(d, 42)
+    bnd, cent = lloyd_max_codebook(d, bits)
+    codes, _ = O.encode(X, R, bnd)
+    codes = codes.astype(np.int64)
+    Qr = (Q.astype(np.float64) @ R.T.astype(np.float64)).astype(np.float32)
+    mq = np.abs(Qr).max(1, keepdims=True)
+    qh, ql = digits(Qr, mq)
+    mc = np.abs(cent).max()
+    ch, cl = digits(cent, mc)
+    HH = qh @ ch[codes].T
+    Xc = qh @ cl[codes].T + ql @ ch[codes].T
+    v = HH + ((Xc + 128) >> 8)
+    xb = (np.abs(qh).sum(1) * np.abs(cl).max() + np.abs(ql).sum(1) * np.abs(ch).max() + 128) >> 8
+    qs = (mq[:, 0] / DIGIT_MAX * (mc / DIGIT_MAX * 65536)).astype(np.float32)
+    f = np.float32
+    for q in range(nq):
+        for g0 in range(0, n, 8):
+            rows = slice(g0, g0 + 8)
+            nr = norms_all[rows]
+            sc = (v[q, rows].astype(f) * qs[q]) * nr
+            for top in (HH[q, rows].max() + xb[q], v[q, rows].max()):
+                b = f(f(top) * qs[q]) * (nr.max() if top >= 0 else nr.min())
+                assert np.all(sc <= b), (q, g0)
+            assert v[q, rows].max() <= HH[q, rows].max() + xb[q]
