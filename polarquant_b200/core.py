@@ -29,6 +29,7 @@ from .device import (alloc_rows, check_device_errors, ptr, require_cuda, row_str
                      rows_to_device, rows_to_host, stream_ptr, to_device_f32, topk_to_numpy,
                      workspace)
 from .packing import pack, packed_nbytes, pack_rows, unpack, unpack_rows
+from .pq_format import read_arrow, read_npz, write_arrow, write_npz
 from .params import haar_rotation, lloyd_max_codebook, nested_codebooks
 
 TOPK_MAX = _lib.PQ_TOPK_MAX
@@ -234,19 +235,18 @@ class CompressedVectors:
         self._x_hat_rot = None
 
     def save(self, path: str) -> None:
-        """Same .npz keys and bytes as remex/core.py:64-74."""
+        """Same .npz keys and arrays as remex/core.py:64-74."""
         if self._rows is not None and (self.d * self.bits) % 8 == 0:
             flat = self._rows.rows_host().ravel()
         else:
             flat = pack(self.indices.ravel(), self.bits)
-        np.savez_compressed(path, packed_indices=flat, norms=self.norms,
-                            d=np.int32(self.d), bits=np.int32(self.bits), n=np.int32(self.n))
+        write_npz(path, flat, self.norms, self.d, self.bits, self.n)
 
     @classmethod
     def load(cls, path: str) -> "CompressedVectors":
         """remex/core.py:76-91 (also reads the legacy unpacked 'indices' key)."""
-        data = np.load(path)
-        d, bits, n = int(data["d"]), int(data["bits"]), int(data["n"])
+        data = read_npz(path)
+        d, bits, n = data["d"], data["bits"], data["n"]
         norms = data["norms"]
         if "packed_indices" in data:
             flat = data["packed_indices"]
@@ -361,54 +361,26 @@ class PackedVectors:
         return (self.n * self.d * 4) / self.nbytes
 
     def save(self, path: str) -> None:
-        """remex/core.py:326-335."""
-        np.savez_compressed(path, packed_indices=self._packed.ravel(), norms=self.norms,
-                            d=np.int32(self.d), bits=np.int32(self.bits), n=np.int32(self.n))
+        """remex/core.py:326-335: the padded rows back to back."""
+        write_npz(path, self._packed.ravel(), self.norms, self.d, self.bits, self.n)
 
     @classmethod
     def load(cls, path: str) -> "PackedVectors":
-        data = np.load(path)
-        d, bits, n = int(data["d"]), int(data["bits"]), int(data["n"])
+        """remex/core.py:337-347."""
+        data = read_npz(path)
+        d, bits, n = data["d"], data["bits"], data["n"]
         rb = packed_nbytes(1, d, bits)
         return cls(data["packed_indices"].reshape(n, rb), data["norms"], n, d, bits)
 
     def save_arrow(self, path: str, seed: Optional[int] = None, **extra_metadata):
-        """Arrow IPC layout of remex/core.py:349-401."""
-        try:
-            import pyarrow as pa
-            import pyarrow.feather as feather
-        except ImportError:
-            raise ImportError("pyarrow is required for Arrow IPC format: pip install pyarrow")
-        meta = {b"d": str(self.d).encode(), b"bits": str(self.bits).encode(),
-                b"n": str(self.n).encode()}
-        if seed is not None:
-            meta[b"seed"] = str(seed).encode()
-        for k, v in extra_metadata.items():
-            meta[k.encode() if isinstance(k, str) else k] = str(v).encode()
-        schema = pa.schema([pa.field("norms", pa.float32()),
-                            pa.field("packed_indices", pa.binary(self._row_bytes))],
-                           metadata=meta)
-        arr = pa.FixedSizeBinaryArray.from_buffers(
-            pa.binary(self._row_bytes), self.n, [None, pa.py_buffer(self._packed.tobytes())])
-        table = pa.table({"norms": pa.array(self.norms, type=pa.float32()),
-                          "packed_indices": arr}, schema=schema)
-        feather.write_feather(table, path)
+        """Arrow IPC (Feather v2) layout of remex/core.py:349-401."""
+        write_arrow(path, self._packed, self.norms, self.d, self.bits, seed, **extra_metadata)
 
     @classmethod
     def load_arrow(cls, path: str, memory_map: bool = False) -> "PackedVectors":
-        try:
-            import pyarrow.feather as feather
-        except ImportError:
-            raise ImportError("pyarrow is required for Arrow IPC format: pip install pyarrow")
-        table = feather.read_table(path, memory_map=memory_map)
-        meta = table.schema.metadata
-        d, bits, n = int(meta[b"d"]), int(meta[b"bits"]), int(meta[b"n"])
-        rb = packed_nbytes(1, d, bits)
-        norms = table.column("norms").to_numpy().astype(np.float32)
-        col = table.column("packed_indices").combine_chunks()
-        flat = np.frombuffer(col.buffers()[1], dtype=np.uint8)[col.offset * rb:
-                                                               (col.offset + n) * rb]
-        return cls(flat.reshape(n, rb).copy(), norms, n, d, bits)
+        """remex/core.py:403-439."""
+        rows, norms, n, d, bits = read_arrow(path, memory_map=memory_map)
+        return cls(rows, norms, n, d, bits)
 
 
 # ---------------------------------------------------------------------------

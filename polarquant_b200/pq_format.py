@@ -1,4 +1,6 @@
-"""The `.pq` and `.params` binary files of the reference (remex/pq_format.py).
+"""The corpus and parameter files of the reference: `.pq` and `.params`
+(remex/pq_format.py), and the host side of the `.npz` and Arrow IPC files of
+CompressedVectors / PackedVectors (remex/core.py:64-116, :326-439).
 
 `.pq` (remex/pq_format.py:3-17, :87-131), little-endian:
 
@@ -117,3 +119,82 @@ def load_pq(path):
     norms = np.frombuffer(raw, dtype="<f4", count=n, offset=PQ_HEADER_BYTES + nbytes)
     codes = unpack(stream, bits, n * d).reshape(n, d)
     return CompressedVectors(codes.copy(), norms.astype(np.float32), d, bits)
+
+
+# ---------------------------------------------------------------------------
+# .npz (remex/core.py:64-91, :326-347) and Arrow IPC / Feather v2
+# (remex/core.py:349-439): the host side of CompressedVectors / PackedVectors
+# .save, .load, .save_arrow and .load_arrow.  The classes hand these the host
+# copies of their rows and norms and build device rows from what they return.
+# ---------------------------------------------------------------------------
+
+def write_npz(path, packed_flat, norms, d: int, bits: int, n: int) -> None:
+    """Keys packed_indices (flat uint8), norms, d, bits, n (int32), compressed."""
+    np.savez_compressed(path, packed_indices=np.ascontiguousarray(packed_flat, np.uint8).ravel(),
+                        norms=norms, d=np.int32(d), bits=np.int32(bits), n=np.int32(n))
+
+
+def read_npz(path) -> dict:
+    """The arrays of a .npz corpus file: d, bits, n, norms, and either
+    packed_indices (flat uint8) or, in files of the older layout, indices
+    (n x d uint8 codes)."""
+    data = np.load(path)
+    out = {"d": int(data["d"]), "bits": int(data["bits"]), "n": int(data["n"]),
+           "norms": data["norms"]}
+    if "packed_indices" in data:
+        out["packed_indices"] = data["packed_indices"]
+    else:
+        out["indices"] = data["indices"]
+    return out
+
+
+def _pyarrow(feather_only: bool = False):
+    try:
+        import pyarrow.feather as feather
+        if feather_only:
+            return None, feather
+        import pyarrow as pa
+    except ImportError:
+        raise ImportError("pyarrow is required for Arrow IPC format: pip install pyarrow")
+    return pa, feather
+
+
+def write_arrow(path, packed_rows, norms, d: int, bits: int, seed=None,
+                **extra_metadata) -> None:
+    """One record batch with columns norms (float32) and packed_indices
+    (FixedSizeBinary of one packed row); d, bits, n, the optional seed and any
+    extra key-value pairs as schema metadata (values as decimal strings)."""
+    pa, feather = _pyarrow()
+    rows = np.ascontiguousarray(packed_rows, np.uint8)
+    n = int(rows.shape[0])
+    rb = packed_nbytes(1, d, bits)
+    if rows.size != n * rb:
+        raise ValueError(f"packed rows size mismatch: got {rows.size}, expected {n * rb}")
+    meta = {b"d": str(d).encode(), b"bits": str(bits).encode(), b"n": str(n).encode()}
+    if seed is not None:
+        meta[b"seed"] = str(seed).encode()
+    for k, v in extra_metadata.items():
+        meta[k.encode() if isinstance(k, str) else k] = str(v).encode()
+    schema = pa.schema([pa.field("norms", pa.float32()),
+                        pa.field("packed_indices", pa.binary(rb))], metadata=meta)
+    col = pa.FixedSizeBinaryArray.from_buffers(pa.binary(rb), n,
+                                               [None, pa.py_buffer(rows.tobytes())])
+    table = pa.table({"norms": pa.array(np.asarray(norms, np.float32), type=pa.float32()),
+                      "packed_indices": col}, schema=schema)
+    feather.write_feather(table, path)
+
+
+def read_arrow(path, memory_map: bool = False):
+    """(packed rows (n x row_bytes uint8), norms (float32), n, d, bits) of a
+    file written by write_arrow or by the reference's save_arrow."""
+    _, feather = _pyarrow(feather_only=True)
+    table = feather.read_table(path, memory_map=memory_map)
+    meta = table.schema.metadata
+    d, bits, n = int(meta[b"d"]), int(meta[b"bits"]), int(meta[b"n"])
+    rb = packed_nbytes(1, d, bits)
+    norms = table.column("norms").to_numpy().astype(np.float32)
+    col = table.column("packed_indices").combine_chunks()
+    if n == 0:
+        return np.zeros((0, rb), np.uint8), norms, n, d, bits
+    flat = np.frombuffer(col.buffers()[1], dtype=np.uint8)[col.offset * rb:(col.offset + n) * rb]
+    return flat.reshape(n, rb).copy(), norms, n, d, bits
