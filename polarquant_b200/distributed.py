@@ -6,10 +6,10 @@ shard on its GPU; queries are replicated.  The exchange steps are exact:
 * ADC / batch top-k: each rank's local top-k (f32 score, global i64 id) is
   all-gathered and merged (score desc, id asc), giving the same ids and
   scores as one GPU holding the whole corpus.
-* Two-stage: round 1 all-gathers the local coarse top-C lists and every rank
-  selects the same global top-C; round 2 has each rank rescore only the
-  candidates it owns at full precision, all-gathers those lists and merges
-  the top-k.  This reproduces the single-GPU result exactly
+* Two-stage: a first exchange all-gathers the local coarse top-C lists and
+  every rank selects the same global top-C; in a second, each rank rescores
+  only the candidates it owns at full precision, all-gathers those lists and
+  merges the top-k.  This reproduces the single-GPU result exactly
   (remex/core.py:638-719 semantics over the whole corpus).
 
 The collectives run on the caller's process group (NCCL over NVLink on a B200
@@ -144,10 +144,10 @@ class ShardedSearch:
         else:
             s = torch.empty((nq, 0), dtype=torch.float32, device=qrot.device)
             i = torch.empty((nq, 0), dtype=torch.int64, device=qrot.device)
-        _, cand = self._gathered_topk(s, i, ck, ck)        # round 1: global top-C ids
+        _, cand = self._gathered_topk(s, i, ck, ck)        # first exchange: global top-C ids
         k_out = min(int(k), ck)
         fs, fi = self.local_rerank(qrot, cand.contiguous(), k_out)  # owned candidates only
-        return self._gathered_topk(fs, fi, k_out, k_out)   # round 2: global top-k
+        return self._gathered_topk(fs, fi, k_out, k_out)   # second exchange: global top-k
 
 
 def to_numpy(s: torch.Tensor, i: torch.Tensor):
