@@ -82,9 +82,10 @@ int pq_encode(const float* X, int64_t n, int d, const float* R, const void* plan
               const float* boundaries, int bits, uint8_t* packed, int64_t ldb, float* norms,
               void* ws, size_t ws_bytes, void* stream);
 
-/* Tensor-core rotation Y = X @ R^T (f32) through the encode GEMM, for large
- * row counts (same workspace as pq_encode).  Used by decode (X_hat_rot @ R,
- * remex/core.py:531) with the planes of R^T. */
+/* Tensor-core rotation Y = X @ R^T (f32) through the encode GEMM, with the
+ * planes that pq_prepare_rotation made of R (same workspace as pq_encode):
+ * the `X @ R.T` of remex/core.py:507 without the coding, for many rows at
+ * once (pq_rotate below is the exact f64-accumulated path for queries). */
 int pq_rotate_tc(const float* X, int64_t n, int d, const void* planes, float* Y, void* ws,
                  size_t ws_bytes, void* stream);
 
