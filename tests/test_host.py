@@ -111,3 +111,104 @@ def test_product_does_not_import_the_oracle():
                 src = open(os.path.join(dirpath, f)).read()
                 mods = re.findall(r"^\s*(?:from|import)\s+(\S+)", src, re.M)
                 assert not any(m.split(".")[0] == "oracle" for m in mods), f
+
+
+# One rejected call per check, for every entry point that computes: the
+# status is PQ_ERR_INVALID (-1) or PQ_ERR_WORKSPACE (-3) and pq_last_error()
+# names the argument.  The fake pointers (16-byte aligned, never dereferenced)
+# show that each check runs before any device work.
+_A = 16  # a fake aligned device address
+
+
+def _abi_bad_calls():
+    P = ctypes.c_void_p
+    a = P(_A)
+    sc = (a, a, a, 1 << 20, None)  # out_scores, out_ids, ws, ws_bytes, stream (scan shapes)
+    return [
+        ("pq_prepare_rotation", (a, 0, a, 1 << 20, None), -1, "d must be positive"),
+        ("pq_prepare_rotation", (a, 64, a, 16, None), -1, "planes buffer too small"),
+        ("pq_prepare_rotation", (a, 64, P(_A + 4), 1 << 24, None), -1, "16-byte aligned"),
+        ("pq_encode", (a, 10, 32, a, a, a, 5, a, 16, a, a, 1 << 20, None), -1, "bits must be"),
+        ("pq_encode", (a, 10, 32, a, a, a, 4, a, 24, a, a, 1 << 20, None), -1, "multiple of 16"),
+        ("pq_encode", (a, 10, 0, a, a, a, 4, a, 16, a, a, 1 << 20, None), -1, "d must be positive"),
+        ("pq_rotate_tc", (a, 10, 0, a, a, a, 1 << 20, None), -1, "d must be positive"),
+        ("pq_rotate_tc", (a, -1, 8, a, a, a, 1 << 20, None), -1, "n must be >= 0"),
+        ("pq_rotate", (a, 4, 0, a, a, None), -1, "d must be positive"),
+        ("pq_rotate", (a, -1, 8, a, a, None), -1, "nq must be >= 0"),
+        ("pq_decode", (a, 16, a, 10, 32, 4, 5, a, a, a, a, 1 << 20, None), -1, "precision must be 1-4"),
+        ("pq_decode", (a, 8, a, 10, 32, 4, 4, a, a, a, a, 1 << 20, None), -1, "ldb too small"),
+        ("pq_adc_scan", (a, 16, a, 10, 32, 4, 4, a, 1, a, 11, 0) + sc, -1, "exceeds n"),
+        ("pq_adc_scan", (a, 16, a, 10, 32, 4, 4, a, 1, a, 0, 0) + sc, -1, "k must be >= 1"),
+        ("pq_adc_scan", (P(_A + 8), 16, a, 10, 32, 4, 4, a, 1, a, 1, 0) + sc, -1,
+         "16-byte aligned"),
+        ("pq_adc_batch", (a, 16, a, 1000, 32, 4, 4, a, 64, a, 257, 0) + sc, -1, "k must be in"),
+        ("pq_adc_batch", (a, 16, a, 1000, 32, 3, 4, a, 64, a, 10, 0) + sc, -1, "precision must be 1-3"),
+        ("pq_adc_batch", (a, 16, a, -5, 32, 4, 4, a, 64, a, 10, 0) + sc, -1, "n must be >= 0"),
+        ("pq_adc_scan_noalloc", (a, 16, a, 10, 32, 4, 4, a, 1, a, 2049, 0, a, a, None), -1,
+         "allocation-free"),
+        ("pq_adc_scan_noalloc", (a, 16, a, 1 << 24, 32, 4, 4, a, 4096, a, 2048, 0, a, a, None),
+         -3, "scratch"),
+        ("pq_twostage", (a, 16, a, 100, 32, 4, 2, a, 1, a, a, 200, 5, 0) + sc, -1, "candidates"),
+        ("pq_twostage", (a, 16, a, 100, 32, 4, 2, a, 1, a, a, 20, 21, 0) + sc, -1, "k must be in"),
+        ("pq_twostage", (a, 16, a, 100, 32, 4, 0, a, 1, a, a, 20, 5, 0) + sc, -1, "precision"),
+        ("pq_rerank", (a, 16, a, 100, 32, 4, a, 1, a, a, 0, 5, 0, a, a, None), -1, "C must be in"),
+        ("pq_rerank", (a, 16, a, 100, 32, 4, a, 1, a, a, 10, 2049, 0, a, a, None), -1,
+         "k must be in"),
+        ("pq_ivf_cell_ids", (a, 16, 10, 32, 4, 17, 0, a, a, None), -1, "n_bits must be 1-16"),
+        ("pq_ivf_cell_ids", (a, 16, 10, 32, 4, 4, 2, a, a, None), -1, "mode must be"),
+        ("pq_ivf_cell_ids", (a, 16, 10, 8, 4, 9, 1, None, a, None), -1, "exceeds d=8"),
+        ("pq_ivf_cell_ids", (a, 16, 10, 32, 5, 4, 0, a, a, None), -1, "bits must be"),
+        ("pq_ivf_probe", (a, 1, 32, 4, 0, a, 17, a, a, None), -1, "nprobe must be in"),
+        ("pq_ivf_probe", (a, 1, 32, 0, 0, a, 1, a, a, None), -1, "n_bits must be 1-16"),
+        ("pq_ivf_search", (a, 16, a, 100, 32, 4, 2, a, 1, a, a, 4, 0, a, a, a, None, None, 4, 65,
+                           20, 5, 1, a, a, a, 1 << 20, None), -1, "splits must be in"),
+        ("pq_ivf_search", (a, 16, a, 100, 32, 4, 2, a, 1, a, a, 4, 0, a, a, a, a, None, 4, 1,
+                           20, 5, 1, a, a, a, 1 << 20, None), -1, "both be given"),
+        ("pq_ivf_search", (a, 16, a, 100, 32, 4, 2, a, 1, a, None, 4, 0, a, a, a, None, None, 4,
+                           1, 20, 5, 1, a, a, a, 1 << 20, None), -1, "full-precision"),
+        ("pq_ivf_search", (a, 16, a, 100, 32, 4, 2, a, 1, a, a, 4, 0, a, a, a, None, None, 4, 1,
+                           20, 5, 1, a, a, a, 64, None), -3, "workspace bytes"),
+        ("pq_unpack_rows", (a, 16, 10, 32, 4, 4, a, None), -1, "shift out of range"),
+        ("pq_unpack_at", (a, 16, a, 3, 32, 4, -1, a, None), -1, "shift out of range"),
+        ("pq_repack", (a, 16, 10, 32, 4, 8, a, 16, None), -1, "target_bits"),
+        ("pq_repack", (a, 16, 10, 32, 4, 2, a, 8, None), -1, "bad ldb_out"),
+        ("pq_pack_codes", (a, 10, 32, 4, a, 8, None), -1, "bad ldb"),
+        ("pq_topk_merge", (a, a, 0, 1, 4, 2, a, a, None), -1, "bad merge shape"),
+    ]
+
+
+@pytest.mark.parametrize("case", range(len(_abi_bad_calls())))
+def test_abi_argument_checks(lib, case):
+    name, args, code, msg = _abi_bad_calls()[case]
+    rc = getattr(lib, name)(*args)
+    assert rc == code, (name, rc, lib.pq_last_error())
+    assert msg.encode() in lib.pq_last_error(), (name, lib.pq_last_error())
+
+
+def test_abi_empty_inputs_do_no_device_work(lib):
+    """Zero queries or zero rows succeed at once (no launch, no device query)."""
+    P = ctypes.c_void_p
+    a = P(_A)
+    before = lib.pq_launch_count()
+    calls = [
+        ("pq_adc_scan", (a, 16, a, 10, 32, 4, 4, None, 0, None, 5, 0, None, None, None, 0, None)),
+        ("pq_adc_batch", (a, 16, a, 10, 32, 4, 4, None, 0, None, 5, 0, None, None, None, 0, None)),
+        ("pq_twostage", (a, 16, a, 100, 32, 4, 2, None, 0, None, None, 20, 5, 0, None, None,
+                         None, 0, None)),
+        ("pq_rerank", (a, 16, a, 100, 32, 4, None, 0, None, None, 10, 5, 0, None, None, None)),
+        ("pq_encode", (None, 0, 32, None, None, None, 4, None, 16, None, None, 0, None)),
+        ("pq_rotate", (None, 0, 32, None, None, None)),
+        ("pq_rotate_tc", (None, 0, 32, None, None, None, 0, None)),
+        ("pq_decode", (None, 16, None, 0, 32, 4, 4, None, None, None, None, 0, None)),
+        ("pq_ivf_cell_ids", (None, 16, 0, 32, 4, 4, 0, None, None, None)),
+        ("pq_ivf_probe", (None, 0, 32, 4, 0, None, 3, None, None, None)),
+        ("pq_unpack_rows", (None, 16, 0, 32, 4, 0, None, None)),
+        ("pq_unpack_at", (None, 16, None, 0, 32, 4, 0, None, None)),
+        ("pq_repack", (None, 16, 0, 32, 4, 2, None, 16, None)),
+        ("pq_pack_codes", (None, 0, 32, 4, None, 16, None)),
+        ("pq_topk_merge", (None, None, 2, 0, 4, 3, None, None, None)),
+    ]
+    for name, args in calls:
+        rc = getattr(lib, name)(*args)
+        assert rc == 0, (name, rc, lib.pq_last_error())
+    assert lib.pq_launch_count() == before
