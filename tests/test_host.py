@@ -212,3 +212,30 @@ def test_abi_empty_inputs_do_no_device_work(lib):
         rc = getattr(lib, name)(*args)
         assert rc == 0, (name, rc, lib.pq_last_error())
     assert lib.pq_launch_count() == before
+
+
+def test_api_errors_match_reference_messages():
+    """The errors the reference raises before any arithmetic (remex/core.py:
+    265-268, :466-472, :563-568, :748-753, :888-891), raised here before any
+    device work, with the same types and messages."""
+    from polarquant_b200 import PackedVectors, Quantizer
+    pq = Quantizer(16, bits=4, seed=42)
+    pv = PackedVectors.__new__(PackedVectors)  # no device rows: the checks come first
+    pv.bits = 4
+    q = np.zeros(16, np.float32)
+    for fn, name in ((pq.search, "search"), (pq.search_batch, "search_batch")):
+        msg = (f"PackedVectors does not support cached {name}(). Use search_adc() or "
+               f"search_twostage(), or convert with packed.to_compressed() first.")
+        with pytest.raises(TypeError, match=re.escape(msg)):
+            fn(pv, q)
+    with pytest.raises(TypeError, match="expected CompressedVectors or PackedVectors"):
+        pq.search_adc(object(), q)
+    for p in (0, 5):
+        with pytest.raises(ValueError, match=re.escape(f"precision must be 1-4, got {p}")):
+            pq._resolve_centroids(None, p)
+    with pytest.raises(ValueError, match=re.escape("target_bits must be 1-4, got 5")):
+        pv.at_precision(5)
+    with pytest.raises(ValueError, match=re.escape("bits must be 1-4 or 8, got 9")):
+        Quantizer(16, bits=9)
+    with pytest.raises(ValueError, match=re.escape("bits=6 is not supported. Use 1-4 or 8 bits.")):
+        Quantizer(16, bits=6)
