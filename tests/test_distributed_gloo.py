@@ -2,8 +2,9 @@
 
 polarquant_b200.distributed.ShardedSearch does the sharding, all-gathers and
 the exact two-round two-stage merge; here its per-rank compute steps are
-replaced by the NumPy oracle so the protocol is checked alone: two ranks must
-return exactly what one process holding the whole corpus returns.  A second
+replaced by the NumPy oracle so the protocol is checked alone: 2, 3 or 4 ranks
+(uneven shards, shards smaller than k, a rank without rows) must return
+exactly what one process holding the whole corpus returns.  A second
 test makes one rank fail before the collective and checks that the survivor
 gets an error from the process-group timeout instead of hanging.
 """
@@ -29,10 +30,10 @@ def _free_port():
     return p
 
 
-def _data():
+def _data(n=1001):
     from oracle import remex_oracle as O
     from polarquant_b200.params import haar_rotation, lloyd_max_codebook, nested_codebooks
-    d, n, bits = 64, 1001, 4
+    d, bits = 64, 4
     rng = np.random.default_rng(0)
     X = rng.standard_normal((n, d)).astype(np.float32)
     Q = rng.standard_normal((5, d)).astype(np.float32)
@@ -48,7 +49,7 @@ def _order(scores, ids, k):
     return scores[o], ids[o]
 
 
-def _rank_main(rank, world, port, outdir):
+def _rank_main(rank, world, port, outdir, n, ka, ck, kt):
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import datetime
@@ -57,7 +58,7 @@ def _rank_main(rank, world, port, outdir):
     from oracle import remex_oracle as O
     from polarquant_b200.core import Quantizer
     from polarquant_b200.distributed import ShardedSearch, shard_bounds
-    d, n, bits, Q, R, cent, nest, idx, norms = _data()
+    d, n, bits, Q, R, cent, nest, idx, norms = _data(n)
     r0, r1 = shard_bounds(n, world, rank)
 
     class Shard:
@@ -105,27 +106,35 @@ def _rank_main(rank, world, port, outdir):
     pq.d, pq.bits, pq.seed = d, bits, 42
     pq.R, pq.centroids, pq._nested = R, cent, nest
     ss = CpuSharded(pq, Shard(r1 - r0), r0, n)
-    a_s, a_i = ss.search_adc_many(Q, k=17, precision=3)
-    t_s, t_i = ss.search_twostage_many(Q, k=7, candidates=50, coarse_precision=2)
+    a_s, a_i = ss.search_adc_many(Q, k=ka, precision=3)
+    t_s, t_i = ss.search_twostage_many(Q, k=kt, candidates=ck, coarse_precision=2)
     np.savez(os.path.join(outdir, f"rank{rank}.npz"), a_s=a_s.numpy(), a_i=a_i.numpy(),
              t_s=t_s.numpy(), t_i=t_i.numpy())
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_sharded_protocol_equals_single_process(tmp_path):
+# (ranks, rows, k, candidates, two-stage k): uneven shards; shards with fewer
+# rows than k (padded with sentinel slots before the exchange); a rank that
+# holds no rows at all.
+@pytest.mark.parametrize("world,n,ka,ck,kt", [(2, 1001, 17, 50, 7), (3, 40, 17, 30, 7),
+                                              (4, 3, 2, 2, 1)])
+def test_sharded_protocol_equals_single_process(tmp_path, world, n, ka, ck, kt):
     from oracle import remex_oracle as O
     port = _free_port()
-    mp.start_processes(_rank_main, args=(2, port, str(tmp_path)), nprocs=2, join=True,
-                       start_method="spawn")
-    d, n, bits, Q, R, cent, nest, idx, norms = _data()
-    r = [np.load(os.path.join(tmp_path, f"rank{k}.npz")) for k in range(2)]
+    mp.start_processes(_rank_main, args=(world, port, str(tmp_path), n, ka, ck, kt),
+                       nprocs=world, join=True, start_method="spawn")
+    d, n, bits, Q, R, cent, nest, idx, norms = _data(n)
+    r = [np.load(os.path.join(tmp_path, f"rank{k}.npz")) for k in range(world)]
     for name in ("a_s", "a_i", "t_s", "t_i"):
-        np.testing.assert_array_equal(r[0][name], r[1][name])  # every rank agrees
+        for k in range(1, world):
+            np.testing.assert_array_equal(r[0][name], r[k][name])  # every rank agrees
+    assert r[0]["a_i"].shape == (len(Q), min(ka, n))
+    assert (r[0]["a_i"] >= 0).all() and (r[0]["t_i"] >= 0).all()
     for qi, q in enumerate(Q):
-        ri, rs = O.search_adc(R, cent, nest, bits, idx, norms, q, k=17, precision=3)
+        ri, rs = O.search_adc(R, cent, nest, bits, idx, norms, q, k=ka, precision=3)
         assert O.topk_equal_up_to_ties(r[0]["a_i"][qi], r[0]["a_s"][qi], ri, rs, rtol=1e-6)
-        ri, rs = O.search_twostage(R, cent, nest, bits, idx, norms, q, k=7, candidates=50,
+        ri, rs = O.search_twostage(R, cent, nest, bits, idx, norms, q, k=kt, candidates=ck,
                                    coarse_precision=2)
         assert O.topk_equal_up_to_ties(r[0]["t_i"][qi], r[0]["t_s"][qi], ri, rs, rtol=1e-6)
 
