@@ -1,7 +1,7 @@
 """Row-sharded search protocol over torch.distributed ranks, on CPU (gloo).
 
 polarquant_b200.distributed.ShardedSearch does the sharding, all-gathers and
-the exact two-round two-stage merge; here its per-rank compute steps are
+the exact two-exchange two-stage merge; here its per-rank compute steps are
 replaced by the NumPy oracle so the protocol is checked alone: 2, 3 or 4 ranks
 (uneven shards, shards smaller than k, a rank without rows) must return
 exactly what one process holding the whole corpus returns.  A second
