@@ -26,7 +26,7 @@ One JSON line on rank 0.  Workloads (synthetic, seeded, generated on the GPU):
   c4s: the c4 kernel on a 4M-row slice (for ncu captures).
 
 Multi-GPU: rows are sharded contiguously across ranks (torch.distributed,
-NCCL); each step runs the exact two-round merge (all-gather of coarse
+NCCL); each step runs the exact two-exchange merge (all-gather of coarse
 candidates, owner rerank, all-gather of fine top-k).  Timing: CUDA events on
 the compute stream, barrier + synchronize around the timed steps, max over
 ranks.

@@ -1,7 +1,7 @@
 """Row-sharded search on 2 GPUs over NCCL (skipped with fewer GPUs): every
 rank's results must equal the single-corpus oracle results, for the streaming
 scan (few queries), the tensor-core batch path (>= 64 queries) and the exact
-two-round two-stage merge."""
+two-exchange two-stage merge."""
 
 import os
 import socket
