@@ -576,16 +576,27 @@ pair_i8_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant_
           const float nr_all = c == 0 ? nrm[0] : c == 1 ? nrm[1] : c == 2 ? nrm[2] : nrm[3];
           const float nmx_c = c == 0 ? nmx[0] : c == 1 ? nmx[1] : c == 2 ? nmx[2] : nmx[3];
           const float nmn_c = c == 0 ? nmn[0] : c == 1 ? nmn[1] : c == 2 ? nmn[2] : nmn[3];
+          // The four groups' first bounds side by side (independent chains),
+          // then one warp-wide OR of the per-thread group masks.
+          float gmx[4], gmn[4];
+          unsigned wbits = 0u;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const float gmax = __shfl_sync(0xffffffffu, nmx_c, 8 * j);
-            const float gmin = __shfl_sync(0xffffffffu, nmn_c, 8 * j);
+            gmx[j] = __shfl_sync(0xffffffffu, nmx_c, 8 * j);
+            gmn[j] = __shfl_sync(0xffffffffu, nmn_c, 8 * j);
             int t4[4];                                 // tree max of the group's 8 HH values
 #pragma unroll
             for (int i = 0; i < 4; ++i) t4[i] = max((int)h[8 * j + i], (int)h[8 * j + i + 4]);
             const int hmax = max(max(t4[0], t4[2]), max(t4[1], t4[3])) + xb;
-            bool want = qv && (__int2float_rn(hmax) * qs) * (hmax >= 0 ? gmax : gmin) > thr;
-            if (!__any_sync(0xffffffffu, want)) continue;
+            if (qv && (__int2float_rn(hmax) * qs) * (hmax >= 0 ? gmx[j] : gmn[j]) > thr)
+              wbits |= 1u << j;
+          }
+          const unsigned groups = __reduce_or_sync(0xffffffffu, wbits);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (!((groups >> j) & 1u)) continue;
+            const float gmax = gmx[j], gmin = gmn[j];
+            bool want = (wbits >> j) & 1u;
             uint32_t x[8];
             __syncwarp();
             tc::tmem_ld8(taddr + (uint32_t)(kQN + 32 * c + 8 * j), x);
