@@ -51,10 +51,26 @@ int pq_version(void);
 /* Message of the last failed call on this thread ("" if none). */
 const char* pq_last_error(void);
 
+/* Codes a kernel records in the device error word when one of its bounded
+ * waits (~2 s of SM clock) runs out: the CTA stops, drains its in-flight
+ * copies and MMAs (bounded), frees its TMEM and returns -- no trap, no hang. */
+#define PQ_DEVICE_ERR_WAIT_TMA_FULL 101    /* a TMA copy never landed */
+#define PQ_DEVICE_ERR_WAIT_STAGE_EMPTY 102 /* a pipeline stage was never released */
+#define PQ_DEVICE_ERR_WAIT_ACC_FULL 103    /* an MMA accumulator never completed */
+#define PQ_DEVICE_ERR_WAIT_ACC_EMPTY 104   /* an accumulator was never drained */
+#define PQ_DEVICE_ERR_WAIT_SELFTEST 105    /* pq_selftest_wait_timeout */
+
 /* Synchronises the current device and reports (then clears) the first
  * device-side failure recorded by a kernel whose bounded wait ran out:
  * *code = 0 when none.  Returns PQ_ERR_CUDA if the synchronisation fails. */
 int pq_device_status(int* code);
+
+/* Self-test of the bounded waits (no counterpart in the reference): one block
+ * waits on an mbarrier that nothing arrives at, through the same wait routine
+ * as the tensor-core kernels but with a limit of `limit_cycles` SM clock
+ * cycles (1e3 .. 4e9).  The wait runs out, PQ_DEVICE_ERR_WAIT_SELFTEST is
+ * recorded for pq_device_status() and the kernel returns normally. */
+int pq_selftest_wait_timeout(int64_t limit_cycles, void* stream);
 
 /* Number of kernels the library has launched in this process (all devices). */
 int64_t pq_launch_count(void);
@@ -143,6 +159,10 @@ int pq_adc_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
  * Same arguments and output as pq_adc_scan; 1 <= k <= 256, k <= n.
  * ------------------------------------------------------------------------- */
 size_t pq_adc_batch_workspace_bytes(int64_t n, int d, int nq, int k);
+/* Which kernel pq_adc_batch runs for this shape: 1 = int8 CTA-pair kernel
+ * (candidates rescored exactly), 2 = fp16 hi/lo CTA-pair kernel, 3 = fp16
+ * one-CTA kernel.  Diagnostic (queries the device's cluster occupancy). */
+int pq_adc_batch_kernel(int64_t n, int d, int bits, int precision, int k, int64_t ldb);
 int pq_adc_batch(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
                  int bits, int precision, const float* qrot, int nq, const float* cent, int k,
                  int64_t row_offset, float* out_scores, int64_t* out_ids, void* ws,
@@ -155,11 +175,17 @@ int pq_adc_batch(const uint8_t* packed, int64_t ldb, const float* norms, int64_t
  * paths that cannot pay for cudaMalloc/cudaFree (which may synchronise the
  * device).  The caller passes only inputs and outputs; the scan's scratch is
  * a built-in device array of pq_adc_scan_noalloc_scratch_bytes() (16 MiB)
- * that every GPU loading the library holds until the process exits.  Calls
- * needing more scratch (many queries x large k) are rejected with
- * PQ_ERR_WORKSPACE; k <= PQ_TOPK_MAX.  The first call on each device looks up
- * the array's device address (cudaGetSymbolAddress) and should come before
- * any stream capture.  All calls on a device share the array, so calls that
+ * that every GPU loading the library holds until the process exits.  A call
+ * is accepted when pq_adc_scan_workspace_bytes(n, d, nq, k) fits in it, else
+ * rejected with PQ_ERR_WORKSPACE (and k > PQ_TOPK_MAX with PQ_ERR_INVALID).
+ * The scan splits the rows into about 8 blocks per SM in total, over all
+ * queries, each keeping k candidates of 12 bytes, so on corpora of more than
+ * about 2.4 million rows the limit is k <= ~16 MiB / (12 * 8 * SMs), i.e.
+ * k <= ~1,180 on a 148-SM B200 whatever the query count; smaller corpora
+ * (fewer blocks) allow k up to PQ_TOPK_MAX.  The first call on each device
+ * (and the first after the device's context is re-created) looks up the
+ * array's device address (cudaGetSymbolAddress) and should come before any
+ * stream capture.  All calls on a device share the array, so calls that
  * overlap on the GPU race and must be serialised by the caller.  Arguments
  * and results are those of pq_adc_scan.
  * ------------------------------------------------------------------------- */
@@ -174,7 +200,9 @@ int pq_adc_scan_noalloc(const uint8_t* packed, int64_t ldb, const float* norms, 
  * (remex/core.py:638-719): coarse ADC at `coarse_precision` over all rows,
  * top-`candidates` (unordered, any tie order), then full-precision rescoring
  * sum_j q_rot[j]*cent_full[code_j]*norm of those rows, top-k.
- * candidates <= PQ_TOPK_MAX, candidates <= n, k <= candidates.
+ * 1 <= candidates <= n, k <= candidates; more than PQ_TOPK_MAX candidates
+ * take a sort-based path one query at a time (every row's coarse score
+ * sorted, the first `candidates` rescored and sorted).
  * cent_coarse: 2^coarse_precision centroids; cent_full: 2^bits centroids.
  * With candidates <= 256, batches of >= 64 queries (>= 8 on corpora of at
  * least 2^20 rows) run the coarse stage on the tensor cores (as
@@ -216,13 +244,28 @@ int pq_rerank(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n,
  *   contiguous run; without them rows are gathered through sorted_idx.  Each
  *   query's probed rows are split into `splits` equal groups, one block and
  *   one candidate list each.  Slots past a query's candidate count hold id -1.
- *   Workspace: pq_ivf_workspace_bytes(nq, nprobe, splits, C).
+ *   candidates (the coarse k of search_coarse) may exceed PQ_TOPK_MAX: such
+ *   calls sort each query's probed rows by coarse score instead of keeping a
+ *   fused top-C, and synchronise `stream` once to read the probed-row counts.
+ *   Workspace: pq_ivf_workspace_bytes(n, nq, nprobe, splits, C).
  * ------------------------------------------------------------------------- */
 int pq_ivf_cell_ids(const uint8_t* packed, int64_t ldb, int64_t n, int d, int bits, int n_bits,
                     int mode, const float* hyperplanes, uint16_t* cells, void* stream);
 int pq_ivf_probe(const float* qrot, int nq, int d, int n_bits, int mode, const float* hyperplanes,
                  int nprobe, int* probe, int* query_cells, void* stream);
-size_t pq_ivf_workspace_bytes(int nq, int nprobe, int splits, int candidates);
+/* CSR layout of the cell ids (remex/ivf.py:216-224: sorted_idx =
+ * argsort(cell_ids, kind="stable"), offsets = [0, cumsum(bincount)]) by a
+ * stable counting sort on the device: sorted_idx (n int64), offsets
+ * (2^n_bits + 1 int64).  With cell_rows/cell_norms (both or neither) the
+ * packed rows (stride ldb, 16-byte aligned) and norms are also copied in CSR
+ * order (the layout pq_ivf_search reads; no reference counterpart).
+ * Workspace: pq_ivf_csr_workspace_bytes(n, n_bits). */
+size_t pq_ivf_csr_workspace_bytes(int64_t n, int n_bits);
+int pq_ivf_build_csr(const uint16_t* cells, int64_t n, int n_bits, int64_t* sorted_idx,
+                     int64_t* offsets, const uint8_t* packed, int64_t ldb, const float* norms,
+                     uint8_t* cell_rows, float* cell_norms, void* ws, size_t ws_bytes,
+                     void* stream);
+size_t pq_ivf_workspace_bytes(int64_t n, int nq, int nprobe, int splits, int candidates);
 int pq_ivf_search(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
                   int bits, int coarse_precision, const float* qrot, int nq,
                   const float* cent_coarse, const float* cent_full, int n_bits, int mode,

@@ -26,6 +26,7 @@ SIGNATURES = {
     "pq_version": (_I, []),
     "pq_last_error": (ctypes.c_char_p, []),
     "pq_device_status": (_I, [ctypes.POINTER(_I)]),
+    "pq_selftest_wait_timeout": (_I, [_L, _P]),
     "pq_row_bytes": (_L, [_I, _I]),
     "pq_launch_count": (_L, []),
     "pq_rotate": (_I, [_P, _L, _I, _P, _P, _P]),
@@ -39,6 +40,7 @@ SIGNATURES = {
     "pq_adc_scan_workspace_bytes": (_Z, [_L, _I, _I, _I]),
     "pq_adc_scan_kernel": (_I, [_L, _I, _I, _I, _I, _I, _L]),
     "pq_adc_batch_workspace_bytes": (_Z, [_L, _I, _I, _I]),
+    "pq_adc_batch_kernel": (_I, [_L, _I, _I, _I, _I, _L]),
     "pq_adc_scan_noalloc_scratch_bytes": (_Z, []),
     "pq_adc_scan_noalloc": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _I, _P, _I, _L, _P, _P, _P]),
     "pq_adc_batch": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _I, _P, _I, _L, _P, _P, _P, _Z, _P]),
@@ -50,7 +52,9 @@ SIGNATURES = {
     "pq_topk_merge": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P]),
     "pq_ivf_cell_ids": (_I, [_P, _L, _L, _I, _I, _I, _I, _P, _P, _P]),
     "pq_ivf_probe": (_I, [_P, _I, _I, _I, _I, _P, _I, _P, _P, _P]),
-    "pq_ivf_workspace_bytes": (_Z, [_I, _I, _I, _I]),
+    "pq_ivf_workspace_bytes": (_Z, [_L, _I, _I, _I, _I]),
+    "pq_ivf_csr_workspace_bytes": (_Z, [_L, _I]),
+    "pq_ivf_build_csr": (_I, [_P, _L, _I, _P, _P, _P, _L, _P, _P, _P, _P, _Z, _P]),
     "pq_ivf_search": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _I, _P, _P, _I, _I, _P, _P, _P, _P,
                            _P, _I, _I, _I, _I, _I, _P, _P, _P, _Z, _P]),
     "pq_unpack_rows": (_I, [_P, _L, _L, _I, _I, _I, _P, _P]),

@@ -513,8 +513,6 @@ class Quantizer:
         if ck >= rows.n:
             # Every row is a candidate: stage 2 alone decides (remex/core.py:701-702).
             return self._scan(rows, qrot, min(k, rows.n), self.bits)
-        if ck > TOPK_MAX:
-            raise NotImplementedError(f"candidates={ck} exceeds the fused limit {TOPK_MAX}")
         K = min(int(k), ck)
         pr = self._params(dev)
         ws = workspace(_lib.query("pq_twostage_workspace_bytes", rows.n, rows.d, nq, ck), dev)

@@ -11,3 +11,4 @@
 #include "batched2.cu"
 #include "ivf.cu"
 #include "noalloc.cu"
+#include "selftest.cu"

@@ -643,6 +643,14 @@ static int run_batched(const uint8_t* packed, int64_t ldb, const float* norms, i
   return PQ_OK;
 }
 
+extern "C" int pq_adc_batch_kernel(int64_t n, int d, int bits, int precision, int k,
+                                   int64_t ldb) {
+  if (i8_eligible(n, d, ldb, bits, k) &&
+      rerank_smem(d, precision, k + kI8Margin, k) <= 227 * 1024 && i8_slots() >= 1)
+    return 1;
+  return (pair_covers(n, bits) && pair_slots() >= 1) ? 2 : 3;
+}
+
 static size_t batched_ws(int64_t n, int d, int nq, int k) {
   if (n <= 0 || nq <= 0 || k <= 0 || d <= 0) return 256;
   const size_t one = batched_ws_1cta(n, d, nq, k);

@@ -13,6 +13,8 @@
 // call.  Calls whose work overlaps on the GPU (different streams, or host
 // threads racing) therefore race on the array and must be serialised by the
 // caller.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -24,22 +26,59 @@ constexpr size_t kNoAllocScratchBytes = (size_t)16 << 20;  // 16 MiB per device
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 // In host code `g_noalloc_scratch` names a host-side shadow, not device memory;
-// the device address is looked up once per device with that device current.
+// the device address is looked up (cudaGetSymbolAddress) with the device
+// current, once per device and context: the cached address is dropped when
+// the device's current context is no longer the one it was taken in (after a
+// cudaDeviceReset the primary context is re-created and the array may live at
+// another address).  The context id comes from the driver (cuCtxGetCurrent,
+// cuCtxGetId), reached through cudaGetDriverEntryPoint.
 static void* g_noalloc_addr[256];
+static unsigned long long g_noalloc_ctx[256];
 static std::mutex g_noalloc_mu;
+
+typedef CUresult (*PfnCtxGetCurrent)(CUcontext*);
+typedef CUresult (*PfnCtxGetId)(CUcontext, unsigned long long*);
+
+// Id of the calling thread's current context, 0 when there is none (or the
+// driver cannot say).
+static unsigned long long current_ctx_id() {
+  static PfnCtxGetCurrent get_current = nullptr;
+  static PfnCtxGetId get_id = nullptr;
+  static bool looked_up = false;
+  if (!looked_up) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<PfnCtxGetCurrent>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PfnCtxGetId>(p);
+    looked_up = true;
+  }
+  if (!get_current || !get_id) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 
 static int noalloc_scratch(void** out) {
   int dev = 0;
   PQ_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 256) return fail(PQ_ERR_CUDA, "device ordinal %d out of range", dev);
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
+  const unsigned long long ctx = current_ctx_id();
+  if (!g_noalloc_addr[dev] || ctx == 0 || ctx != g_noalloc_ctx[dev]) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr)
       return fail(PQ_ERR_CUDA, "cudaGetSymbolAddress of the scan scratch failed: %s",
                   cudaGetErrorString(e));
     g_noalloc_addr[dev] = p;
+    g_noalloc_ctx[dev] = current_ctx_id();  // the lookup above made the context current
   }
   *out = g_noalloc_addr[dev];
   return PQ_OK;

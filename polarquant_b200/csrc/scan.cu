@@ -324,6 +324,13 @@ static int adc_large_k(const uint8_t* packed, int64_t ldb, const float* norms, i
                        int k, int64_t row_offset, float* out_s, int64_t* out_ids, void* ws,
                        cudaStream_t st);
 
+// Two-stage search with more than PQ_TOPK_MAX candidates (sort.cu).
+static size_t large_twostage_ws(int64_t n, int C);
+static int large_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
+                          int bits, int cp, const float* qrot, int nq, const float* cent_coarse,
+                          const float* cent_full, int C, int k, int64_t row_offset, float* out_s,
+                          int64_t* out_ids, void* ws, cudaStream_t st);
+
 extern "C" {
 
 size_t pq_adc_scan_workspace_bytes(int64_t n, int d, int nq, int k) {
@@ -392,6 +399,7 @@ static size_t twostage_exact_offset(int64_t n, int d, int nq, int candidates) {
 }
 
 size_t pq_twostage_workspace_bytes(int64_t n, int d, int nq, int candidates) {
+  if (candidates > PQ_TOPK_MAX) return large_twostage_ws(n, candidates);
   const size_t a = pq_adc_scan_workspace_bytes(n, d, nq, candidates);
   if (twostage_batched(n, nq, candidates)) {
     const size_t b = twostage_exact_offset(n, d, nq, candidates) +
@@ -439,15 +447,19 @@ int pq_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
   if (rc) return rc;
   PQ_CHECK_ARG(coarse_precision >= 1 && coarse_precision <= bits,
                "precision must be 1-%d, got %d", bits, coarse_precision);
-  PQ_CHECK_ARG(candidates >= 1 && candidates <= PQ_TOPK_MAX && candidates <= n,
-               "candidates must be in [1, min(n, %d)] (got %d)", PQ_TOPK_MAX, candidates);
+  PQ_CHECK_ARG(candidates >= 1 && candidates <= n,
+               "candidates must be in [1, n] (got %d)", candidates);
   PQ_CHECK_ARG(k >= 1 && k <= candidates, "k must be in [1, candidates] (got %d)", k);
+  PQ_CHECK_ARG(n < (1ll << 31), "n=%lld rows exceed one launch; shard the corpus", (long long)n);
   if (nq == 0) return PQ_OK;
   PQ_CHECK_ARG(qrot && cent_coarse && cent_full && out_scores && out_ids, "null pointer argument");
   const size_t need = pq_twostage_workspace_bytes(n, d, nq, candidates);
   if (ws_bytes < need || !ws)
     return fail(PQ_ERR_WORKSPACE, "pq_twostage needs %zu workspace bytes, got %zu", need, ws_bytes);
   cudaStream_t st = (cudaStream_t)stream;
+  if (candidates > PQ_TOPK_MAX)
+    return large_twostage(packed, ldb, norms, n, d, bits, coarse_precision, qrot, nq, cent_coarse,
+                          cent_full, candidates, k, row_offset, out_scores, out_ids, ws, st);
   float* cs;
   long long* ci;
   int nblk;

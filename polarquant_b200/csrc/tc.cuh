@@ -9,12 +9,14 @@
 namespace pqb {
 namespace tc {
 
-// Error codes written to g_device_error when a bounded wait gives up.
+// Error codes written to g_device_error when a bounded wait gives up (the
+// PQ_DEVICE_ERR_* values of the public header).
 enum : int {
-  kErrWaitTmaFull = 101,
-  kErrWaitStageEmpty = 102,
-  kErrWaitAccFull = 103,
-  kErrWaitAccEmpty = 104,
+  kErrWaitTmaFull = PQ_DEVICE_ERR_WAIT_TMA_FULL,
+  kErrWaitStageEmpty = PQ_DEVICE_ERR_WAIT_STAGE_EMPTY,
+  kErrWaitAccFull = PQ_DEVICE_ERR_WAIT_ACC_FULL,
+  kErrWaitAccEmpty = PQ_DEVICE_ERR_WAIT_ACC_EMPTY,
+  kErrWaitSelftest = PQ_DEVICE_ERR_WAIT_SELFTEST,
 };
 
 // A wait that has not completed after this many SM clock cycles (~2 s at
@@ -62,20 +64,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Waits for the phase of `parity` to complete.  Returns false (and records
 // `err` once per CTA through *abort and g_device_error) if the wait exceeds
-// kWaitCycles or another role of the CTA has already aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
-                                          int err) {
+// `limit` SM clock cycles or another role of the CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait_limit(uint32_t bar, uint32_t parity,
+                                                volatile int* abort, int err, long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       *abort = err;
       device_fail(err);
       return false;
     }
   }
+}
+
+// mbar_wait_limit with the library's limit, kWaitCycles.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                                          int err) {
+  return mbar_wait_limit(bar, parity, abort, err, kWaitCycles);
 }
 
 // 2-D tiled TMA load of box {x: inner, y: rows} into shared memory,

@@ -1,10 +1,11 @@
 """B200 drop-in for remex.ivf.IVFCoarseIndex (remex/ivf.py:65-472).
 
 Same constructor, attributes, methods, results and errors.  The index is
-built on the GPU (cell ids by ivf_cell_ids_kernel; the CSR layout by a stable
-device sort) and kept there; the query path (query cell, Hamming-ranked probe
-cells, gather-ADC over the probed cells' rows, top-C, full-precision rerank)
-runs as one library call per query batch (pq_ivf_search).  Host views
+built on the GPU (cell ids by ivf_cell_ids_kernel; the CSR layout by the
+library's stable counting sort, pq_ivf_build_csr) and kept there; the query
+path (query cell, Hamming-ranked probe cells, gather-ADC over the probed
+cells' rows, top-C, full-precision rerank) runs as one library call per
+query batch (pq_ivf_search).  Host views
 (``cell_ids``, ``sorted_idx``, ``cell_offsets``) are produced on demand.
 
 LSH projections are summed exactly (f64) on the device; the reference sums
@@ -21,7 +22,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from .core import CompressedVectors, PackedVectors, Quantizer, TOPK_MAX
+from .core import CompressedVectors, PackedVectors, Quantizer
 from .device import ptr, stream_ptr, to_device_f32, workspace
 
 _VALID_MODES = ("lsh", "rotated_prefix")
@@ -65,40 +66,35 @@ class IVFCoarseIndex:
         self._H = None if self.hyperplanes is None else \
             torch.from_numpy(self.hyperplanes).to(dev)
         cells = torch.empty(rows.n, dtype=torch.int16, device=dev)
+        st = stream_ptr(dev)
         if rows.n:
             _lib.call("pq_ivf_cell_ids", ptr(rows.buf), rows.ldb, rows.n, rows.d, rows.bits,
-                      self.n_bits, 0 if self.mode == "lsh" else 1, ptr(self._H), ptr(cells),
-                      stream_ptr(dev))
-        cid = cells.view(torch.int16).to(torch.int32) & 0xFFFF
+                      self.n_bits, 0 if self.mode == "lsh" else 1, ptr(self._H), ptr(cells), st)
         # CSR: rows grouped by cell, ascending row order within a cell
-        # (remex/ivf.py:216-224: stable argsort + bincount offsets).
-        self._sorted = torch.sort(cid, stable=True).indices.to(torch.int64)
-        counts = torch.bincount(cid, minlength=self.n_cells)
-        off = torch.zeros(self.n_cells + 1, dtype=torch.int64, device=dev)
-        off[1:] = torch.cumsum(counts, 0)
-        self._offsets = off
-        self._cells = cid
-        self._h_cells = self._h_sorted = self._h_offsets = None
-        sizes = counts.max().item() if rows.n else 0
-        self._max_cell = int(sizes)
-        # The packed rows and norms copied in CSR order (cell by cell), so the
-        # query path reads each probed cell as one contiguous run instead of
-        # gathering rows through sorted_idx.  Costs one more copy of the
-        # corpus on the device.
+        # (remex/ivf.py:216-224: stable argsort + bincount offsets), by the
+        # library's stable counting sort, together with a copy of the packed
+        # rows and norms in CSR order, so the query path reads each probed
+        # cell as one contiguous run instead of gathering rows through
+        # sorted_idx (one more device copy of the corpus).
+        self._sorted = torch.empty(rows.n, dtype=torch.int64, device=dev)
+        self._offsets = torch.empty(self.n_cells + 1, dtype=torch.int64, device=dev)
         if rows.n:
-            src = rows.buf[: rows.n * rows.ldb].view(rows.n, rows.ldb)
             self._cell_rows = torch.zeros(rows.n * rows.ldb + 64, dtype=torch.uint8, device=dev)
-            self._cell_rows[: rows.n * rows.ldb].view(rows.n, rows.ldb).copy_(
-                src.index_select(0, self._sorted))
-            self._cell_norms = rows.norms.index_select(0, self._sorted).contiguous()
+            self._cell_norms = torch.empty(rows.n, dtype=torch.float32, device=dev)
         else:
             self._cell_rows = self._cell_norms = None
+        ws = workspace(_lib.query("pq_ivf_csr_workspace_bytes", rows.n, self.n_bits), dev)
+        _lib.call("pq_ivf_build_csr", ptr(cells), rows.n, self.n_bits, ptr(self._sorted),
+                  ptr(self._offsets), ptr(rows.buf), rows.ldb, ptr(rows.norms),
+                  ptr(self._cell_rows), ptr(self._cell_norms), ptr(ws), ws.numel(), st)
+        self._cells = cells
+        self._h_cells = self._h_sorted = self._h_offsets = None
 
     # -- host views (remex/ivf.py:81-89 attributes) ---------------------------
     @property
     def cell_ids(self) -> np.ndarray:
         if self._h_cells is None:
-            self._h_cells = self._cells.cpu().numpy().astype(np.uint16)
+            self._h_cells = self._cells.cpu().numpy().view(np.uint16)
         return self._h_cells
 
     @property
@@ -163,15 +159,19 @@ class IVFCoarseIndex:
         Qr = q._rotate(queries, dev)
         nq = Qr.shape[0]
         nprobe = int(min(max(nprobe, 0), self.n_cells))
-        if nprobe <= 0 or rows.n == 0 or nq == 0:
+        if nprobe <= 0 or rows.n == 0 or nq == 0 or candidates <= 0 or k <= 0:
+            # No probed cell, no rows or nothing asked for: empty results, as
+            # remex/ivf.py:301-436 returns for an empty candidate set.
             return (np.full((nq, 0), -1, np.int64), np.zeros((nq, 0), np.float32))
-        C = int(min(candidates, TOPK_MAX))
+        # More than the fused limit (TOPK_MAX) candidates take the library's
+        # sort-based path; the result has min(k, candidates) columns either way.
+        C = int(min(candidates, rows.n))
         K = int(min(k, C))
         # Row groups per query: about 8k probed rows each (at least one).
         probed = nprobe * (rows.n / self.n_cells)
         splits = int(min(64, max(1, round(probed / 8192))))
         pr = q._params(dev)
-        ws = workspace(_lib.query("pq_ivf_workspace_bytes", nq, nprobe, splits, C), dev)
+        ws = workspace(_lib.query("pq_ivf_workspace_bytes", rows.n, nq, nprobe, splits, C), dev)
         out_s = torch.empty((nq, K), dtype=torch.float32, device=dev)
         out_i = torch.empty((nq, K), dtype=torch.int64, device=dev)
         _lib.call("pq_ivf_search", ptr(rows.buf), rows.ldb, ptr(rows.norms), rows.n, rows.d,
@@ -197,8 +197,6 @@ class IVFCoarseIndex:
     def search_coarse(self, query, k: int = 500, nprobe: int = 1,
                       precision: Optional[int] = None, chunk_size: int = 4096):
         """remex/ivf.py:301-374."""
-        if k > TOPK_MAX:
-            raise NotImplementedError(f"k={k} exceeds {TOPK_MAX}")
         ids, sc = self.search_coarse_many(np.asarray(query, np.float32)[None], k=k,
                                           nprobe=nprobe, precision=precision)
         return self._trim(ids[0], sc[0])
@@ -208,8 +206,6 @@ class IVFCoarseIndex:
         if coarse_precision is None:
             coarse_precision = max(1, self.quantizer.bits - 2)
         cp = self.quantizer._level(coarse_precision)
-        if candidates > TOPK_MAX:
-            raise NotImplementedError(f"candidates={candidates} exceeds {TOPK_MAX}")
         return self._run(queries, k, nprobe, cp, True, candidates)
 
     def search_twostage(self, query, k: int = 10, candidates: int = 500, nprobe: int = 1,

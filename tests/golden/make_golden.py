@@ -2,7 +2,7 @@
 
 Run from the repository root with the reference checked out read-only:
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py /root/reference
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py <reference checkout>
 
 It imports the reference (pure NumPy/SciPy) and records its outputs on seeded
 inputs: parameters (rotation, codebooks, nested tables), encode results,
@@ -166,4 +166,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {os.path.relpath(__file__)} <path of the reference checkout>")
+    main(sys.argv[1])

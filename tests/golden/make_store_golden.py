@@ -2,7 +2,7 @@
 
 Run from the repository root with the reference checked out read-only:
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_store_golden.py /root/reference
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_store_golden.py <reference checkout>
 
 For each width and two shapes (d=13: rows that are not a whole number of
 bytes at 1-4 bits; d=16: whole-byte rows) it writes seeded codes and norms
@@ -53,4 +53,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {os.path.relpath(__file__)} <path of the reference checkout>")
+    main(sys.argv[1])

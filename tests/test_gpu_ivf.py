@@ -131,3 +131,70 @@ def test_ivf_edges_and_diagnostics(gpu):
     assert ix.index_nbytes > 0 and ix.candidate_count(q, 3) >= 0
     rp = IVFCoarseIndex(pq, cv, n_bits=6, mode="rotated_prefix")
     assert rp.index_nbytes < IVFCoarseIndex(pq, cv, n_bits=6, mode="lsh").index_nbytes
+
+
+@pytest.mark.parametrize("mode", ["lsh", "rotated_prefix"])
+def test_ivf_more_than_2048_candidates_and_k(gpu, mode):
+    """remex/ivf.py:301-436 takes any k / candidate count: above the fused
+    limit the probed rows are sorted by coarse score instead."""
+    from polarquant_b200 import CompressedVectors, IVFCoarseIndex, Quantizer
+    d, n, nb = 128, 40000, 6
+    rng = np.random.default_rng(8)
+    X = unit_rows(rng, n, d)
+    Q = unit_rows(rng, 3, d)
+    pq = Quantizer(d, bits=4, seed=42)
+    idx, norms = O.encode(X, pq.R, pq.boundaries)
+    ix = IVFCoarseIndex(pq, CompressedVectors(idx, norms, d, 4), n_bits=nb, mode=mode, seed=0)
+    H, srt, off = ix.hyperplanes, ix.sorted_idx, ix.cell_offsets
+    for q in Q:
+        gi, gs = ix.search_coarse(q, k=3000, nprobe=7, precision=2)
+        ri, rs = O.ivf_search_coarse(pq.R, pq.centroids, pq._nested, 4, idx, norms, srt, off, nb,
+                                     mode, H, q, k=3000, nprobe=7, precision=2)
+        assert O.topk_equal_up_to_ties(gi, gs, ri, rs, rtol=RTOL)
+        gi, gs = ix.search_twostage(q, k=2100, candidates=5000, nprobe=9, coarse_precision=1)
+        ri, rs = O.ivf_search_twostage(pq.R, pq.centroids, pq._nested, 4, idx, norms, srt, off,
+                                       nb, mode, H, q, k=2100, candidates=5000, nprobe=9,
+                                       coarse_precision=1)
+        assert O.topk_equal_up_to_ties(gi, gs, ri, rs, rtol=RTOL)
+        # One probed cell of fewer rows than asked for: every row, -1 slots trimmed.
+        gi, gs = ix.search_twostage(q, k=10, candidates=4000, nprobe=1)
+        ri, rs = O.ivf_search_twostage(pq.R, pq.centroids, pq._nested, 4, idx, norms, srt, off,
+                                       nb, mode, H, q, k=10, candidates=4000, nprobe=1)
+        assert O.topk_equal_up_to_ties(gi, gs, ri, rs, rtol=RTOL)
+    i, s = ix.search_twostage(Q[0], k=10, candidates=0, nprobe=3)
+    assert i.shape == (0,) and s.shape == (0,)
+
+
+@pytest.mark.parametrize("n,nb", [(50000, 12), (70001, 14), (40000, 15), (30000, 16), (5, 3)])
+def test_ivf_csr_build_matches_stable_argsort(gpu, n, nb):
+    """pq_ivf_build_csr (stable counting sort on the device) against
+    remex/ivf.py:216-224 (argsort kind='stable', bincount, cumsum), for cell
+    counts that use the shared-memory counters (<= 2^14 cells) and the global
+    ones, with skewed cell sizes, and the CSR-order copy of rows and norms."""
+    import torch
+    from polarquant_b200 import _lib
+    from polarquant_b200.device import ptr, stream_ptr, workspace
+    rng = np.random.default_rng(nb)
+    n_cells = 1 << nb
+    # Skewed: half the rows in a few cells, the rest spread out.
+    cells = np.where(rng.random(n) < 0.5, rng.integers(0, 7, n),
+                     rng.integers(0, n_cells, n)).astype(np.uint16)
+    ldb = 32
+    rows = rng.integers(0, 256, size=(n, ldb), dtype=np.uint8)
+    norms = rng.random(n).astype(np.float32)
+    dev = torch.device("cuda")
+    c_d = torch.from_numpy(cells.view(np.int16)).to(dev)
+    r_d = torch.from_numpy(rows.ravel()).to(dev)
+    n_d = torch.from_numpy(norms).to(dev)
+    srt = torch.empty(n, dtype=torch.int64, device=dev)
+    off = torch.empty(n_cells + 1, dtype=torch.int64, device=dev)
+    cr = torch.empty(n * ldb, dtype=torch.uint8, device=dev)
+    cn = torch.empty(n, dtype=torch.float32, device=dev)
+    ws = workspace(_lib.query("pq_ivf_csr_workspace_bytes", n, nb), dev)
+    _lib.call("pq_ivf_build_csr", ptr(c_d), n, nb, ptr(srt), ptr(off), ptr(r_d), ldb, ptr(n_d),
+              ptr(cr), ptr(cn), ptr(ws), ws.numel(), stream_ptr(dev))
+    ref_s, ref_o = O.ivf_csr(cells, n_cells)
+    np.testing.assert_array_equal(srt.cpu().numpy(), ref_s)
+    np.testing.assert_array_equal(off.cpu().numpy(), ref_o)
+    np.testing.assert_array_equal(cr.cpu().numpy().reshape(n, ldb), rows[ref_s])
+    np.testing.assert_array_equal(cn.cpu().numpy(), norms[ref_s])

@@ -363,3 +363,18 @@ def test_small_batch_on_large_corpus_uses_tensor_cores(gpu):
     for q in range(nq):
         ri, rs = O.search_adc(pq.R, pq.centroids, pq._nested, 4, idx, norms, qs[q], k=k)
         assert O.topk_equal_up_to_ties(GI[q], GS[q], ri, rs, rtol=RTOL), q
+
+
+@pytest.mark.parametrize("bits,cands,k,cp", [(4, 5000, 3000, 2), (8, 2500, 10, 4),
+                                             (8, 2049, 2049, None)])
+def test_twostage_more_than_2048_candidates(gpu, bits, cands, k, cp):
+    """remex/core.py:701-704 takes any candidate count: more than the fused
+    top-k limit runs the sort-based path (coarse keys of every row sorted,
+    the first C rescored at full precision and sorted)."""
+    pq, cv, idx, norms, qs = make_case(bits, d=96, n=12000, nq=3)
+    GI, GS = pq.search_twostage_many(cv, qs, k=k, candidates=cands, coarse_precision=cp)
+    assert GI.shape == (3, min(k, cands))
+    for q in range(3):
+        ri, rs = O.search_twostage(pq.R, pq.centroids, pq._nested, bits, idx, norms, qs[q], k=k,
+                                   candidates=cands, coarse_precision=cp)
+        assert_topk(GI[q], GS[q], ri, rs)

@@ -64,6 +64,10 @@ def test_abi_rejects_bad_arguments_before_touching_the_device(lib):
     assert rc == -1 and b"candidates" in lib.pq_last_error()
     with pytest.raises(_lib.PQError):
         _lib.call("pq_topk_merge", P(16), P(16), 2, 1, 4, 9, P(16), P(16), None)
+    # The bounded-wait self-test checks its limit before launching anything.
+    assert lib.pq_selftest_wait_timeout(10, None) == -1
+    assert b"limit_cycles" in lib.pq_last_error()
+    assert lib.pq_selftest_wait_timeout(5_000_000_000, None) == -1
 
 
 def test_quantizer_bit_validation():

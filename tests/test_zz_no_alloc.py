@@ -68,6 +68,11 @@ def test_noalloc_scan_matches_workspace_scan_twice(gpu):
     qrot = pq._rotate(Q, dev)
     ref1, got1 = _both(pq, cv, qrot, 10, 4)
     _same(ref1, got1)
+    # ... and the oracle's search_adc (remex/core.py:582-636) on the same corpus.
+    idx, norms = cv.indices, cv.norms
+    for q in range(Q.shape[0]):
+        ri, rs = O.search_adc(pq.R, pq.centroids, pq._nested, 4, idx, norms, Q[q], k=10)
+        assert O.topk_equal_up_to_ties(got1[0][q], got1[1][q], ri, rs, rtol=RTOL), q
     # Second call in a row: other queries, other k and precision, same scratch.
     qrot2 = pq._rotate(Q[::-1].copy() * 2.0, dev)
     ref2, got2 = _both(pq, cv, qrot2, 37, 2)
@@ -90,3 +95,37 @@ def test_noalloc_scan_rejects_oversized_calls(gpu):
         _lib.call("pq_adc_scan_noalloc", P(rows.buf.data_ptr()), rows.ldb,
                   P(rows.norms.data_ptr()), rows.n, rows.d, rows.bits, 4, P(16), 1, P(16),
                   4096, 0, P(16), P(16), None)
+
+
+def test_noalloc_scan_k_limit_on_a_large_corpus(gpu):
+    """One query on a corpus of a few million rows: the scan then splits the
+    rows into about 8 blocks per SM, so the built-in scratch bounds k well
+    below PQ_TOPK_MAX.  The largest k whose workspace fits is accepted (and
+    matches pq_adc_scan), the next one is rejected with PQ_ERR_WORKSPACE."""
+    import torch
+    from polarquant_b200 import CompressedVectors, Quantizer, _lib
+    d, n = 64, 3_000_000
+    pq = Quantizer(d, bits=4, seed=5)
+    rng = np.random.default_rng(9)
+    idx = rng.integers(0, 16, size=(n, d), dtype=np.uint8)
+    norms = rng.uniform(0.5, 2.0, n).astype(np.float32)
+    cv = CompressedVectors(idx, norms, d, 4)
+    cap = _lib.query("pq_adc_scan_noalloc_scratch_bytes")
+    kmax = 1
+    while kmax < 2048 and _lib.query("pq_adc_scan_workspace_bytes", n, d, 1, kmax + 1) <= cap:
+        kmax += 1
+    assert kmax < 2048, "a multi-million-row corpus should bound k below PQ_TOPK_MAX"
+    q = rng.standard_normal((1, d)).astype(np.float32)
+    dev = cv._device().device
+    qrot = pq._rotate(q, dev)
+    ref, got = _both(pq, cv, qrot, kmax, 4)
+    _same(ref, got)
+    rows = cv._device()
+    s = torch.empty((1, kmax + 1), dtype=torch.float32, device=dev)
+    i = torch.empty((1, kmax + 1), dtype=torch.int64, device=dev)
+    from polarquant_b200.device import ptr, stream_ptr
+    with pytest.raises(_lib.PQError, match="scratch") as e:
+        _lib.call("pq_adc_scan_noalloc", ptr(rows.buf), rows.ldb, ptr(rows.norms), rows.n, d, 4,
+                  4, ptr(qrot), 1, ptr(pq._params(dev).cent[4]), kmax + 1, 0, ptr(s), ptr(i),
+                  stream_ptr(dev))
+    assert e.value.code == -3
