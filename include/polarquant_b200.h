@@ -275,6 +275,32 @@ int pq_ivf_search(const uint8_t* packed, int64_t ldb, const float* norms, int64_
                   void* ws, size_t ws_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * 1-bit popcount coarse scorer.  The reference recommends this coarse tier
+ * for very large corpora (bench/RESULTS.md:153-161: "popcount(query_signs
+ * XOR coarse_signs) -- no Lloyd-Max lookup needed") but ships no code for
+ * it, so its semantics are defined here:
+ *   score(row) = d - 2 * popcount(query_signs XOR row_signs), an integer in
+ *   [-d, d] (the +-1 inner product of the sign vectors), where row_signs are
+ *   the MSBs of the row's codes (its 1-bit Matryoshka level) and query bit j
+ *   is q_rot[j] > 0; top-k by score descending, ties by row ascending.
+ * signs: the corpus's 1-bit rows (MSB-first bits, e.g. pq_repack to 1 bit),
+ * stride ldb (a multiple of 16, >= ceil(d / 128) * 16).  k <= PQ_TOPK_MAX.
+ * pq_hamming_twostage: the top `candidates` (<= PQ_TOPK_MAX) by that score,
+ * rescored at full precision as pq_twostage's second stage
+ * (remex/core.py:706-719), top-k.  Workspace:
+ * pq_hamming_workspace_bytes(n, nq, k or candidates).
+ * ------------------------------------------------------------------------- */
+size_t pq_hamming_workspace_bytes(int64_t n, int nq, int k);
+int pq_hamming_scan(const uint8_t* signs, int64_t ldb, int64_t n, int d, const float* qrot,
+                    int nq, int k, int64_t row_offset, float* out_scores, int64_t* out_ids,
+                    void* ws, size_t ws_bytes, void* stream);
+int pq_hamming_twostage(const uint8_t* signs, int64_t ldb_signs, const uint8_t* packed,
+                        int64_t ldb, const float* norms, int64_t n, int d, int bits,
+                        const float* qrot, int nq, const float* cent_full, int candidates, int k,
+                        int64_t row_offset, float* out_scores, int64_t* out_ids, void* ws,
+                        size_t ws_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Merge of per-part top-k lists: in_s/in_ids are parts x nq x kin (as written
  * by the per-rank scans, ids already global); out is nq x k, k <= kin*parts,
  * k <= PQ_TOPK_MAX.  Used after the NCCL all-gather of the row-sharded search.

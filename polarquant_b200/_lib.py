@@ -57,6 +57,10 @@ SIGNATURES = {
     "pq_ivf_build_csr": (_I, [_P, _L, _I, _P, _P, _P, _L, _P, _P, _P, _P, _Z, _P]),
     "pq_ivf_search": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _I, _P, _P, _I, _I, _P, _P, _P, _P,
                            _P, _I, _I, _I, _I, _I, _P, _P, _P, _Z, _P]),
+    "pq_hamming_workspace_bytes": (_Z, [_L, _I, _I]),
+    "pq_hamming_scan": (_I, [_P, _L, _L, _I, _P, _I, _I, _L, _P, _P, _P, _Z, _P]),
+    "pq_hamming_twostage": (_I, [_P, _L, _P, _L, _P, _L, _I, _I, _P, _I, _P, _I, _I, _L, _P, _P,
+                                 _P, _Z, _P]),
     "pq_unpack_rows": (_I, [_P, _L, _L, _I, _I, _I, _P, _P]),
     "pq_unpack_at": (_I, [_P, _L, _P, _L, _I, _I, _I, _P, _P]),
     "pq_repack": (_I, [_P, _L, _L, _I, _I, _I, _P, _L, _P]),

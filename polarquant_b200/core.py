@@ -59,11 +59,21 @@ BATCH_MAX_K = 256    # largest k of the tensor-core path
 class _DeviceRows:
     """Packed rows (stride ldb) + f32 norms on one CUDA device."""
 
-    __slots__ = ("buf", "norms", "n", "d", "bits", "ldb", "device")
+    __slots__ = ("buf", "norms", "n", "d", "bits", "ldb", "device", "_signs")
 
     def __init__(self, buf, norms, n, d, bits, ldb, device):
         self.buf, self.norms, self.n, self.d = buf, norms, int(n), int(d)
         self.bits, self.ldb, self.device = int(bits), int(ldb), device
+        self._signs = None
+
+    def sign_tier(self) -> "_DeviceRows":
+        """The 1-bit Matryoshka level (the MSB of every code) as packed rows,
+        made once by pq_repack and kept: the popcount scorer's input."""
+        if self.bits == 1:
+            return self
+        if self._signs is None:
+            self._signs = self.at_precision(1)
+        return self._signs
 
     @classmethod
     def from_codes(cls, indices: np.ndarray, norms: np.ndarray, d: int, bits: int):
@@ -568,6 +578,71 @@ class Quantizer:
         self._check_corpus(rows)
         s, i = self._twostage(rows, self._rotate(queries, rows.device), k, candidates, cp)
         return topk_to_numpy(s, i)
+
+    # -- 1-bit popcount coarse scorer (no method of the reference; the coarse
+    # tier its docs recommend, bench/RESULTS.md:153-161) ------------------------
+    def _popcount(self, rows: _DeviceRows, qrot: torch.Tensor, k: int,
+                  candidates: Optional[int] = None):
+        dev = rows.device
+        nq = qrot.shape[0]
+        K = min(int(k), rows.n)
+        C = None if candidates is None else min(int(candidates), rows.n)
+        if K <= 0 or nq == 0 or (C is not None and C <= 0):
+            return (torch.empty((nq, 0), dtype=torch.float32, device=dev),
+                    torch.empty((nq, 0), dtype=torch.int64, device=dev))
+        if C is not None and C >= rows.n:
+            # Every row is a candidate: the full-precision stage alone decides.
+            return self._scan(rows, qrot, K, self.bits)
+        if C is not None:
+            K = min(K, C)
+        width = K if C is None else C
+        if width > TOPK_MAX:
+            raise ValueError(f"the popcount scorer keeps at most {TOPK_MAX} results per query "
+                             f"(asked for {width})")
+        sg = rows.sign_tier()
+        ws = workspace(_lib.query("pq_hamming_workspace_bytes", rows.n, nq, width), dev)
+        out_s = torch.empty((nq, K), dtype=torch.float32, device=dev)
+        out_i = torch.empty((nq, K), dtype=torch.int64, device=dev)
+        if C is None:
+            _lib.call("pq_hamming_scan", ptr(sg.buf), sg.ldb, rows.n, rows.d, ptr(qrot), nq, K,
+                      0, ptr(out_s), ptr(out_i), ptr(ws), ws.numel(), stream_ptr(dev))
+        else:
+            cent = self._params(dev).cent[self.bits]
+            _lib.call("pq_hamming_twostage", ptr(sg.buf), sg.ldb, ptr(rows.buf), rows.ldb,
+                      ptr(rows.norms), rows.n, rows.d, rows.bits, ptr(qrot), nq, ptr(cent), C, K,
+                      0, ptr(out_s), ptr(out_i), ptr(ws), ws.numel(), stream_ptr(dev))
+        return out_s, out_i
+
+    def search_popcount_many(self, compressed, queries, k: int = 10):
+        """Coarse search by 1-bit sign agreement: score = d - 2 * popcount(
+        query_signs XOR row_signs), the row signs being the MSBs of its codes
+        and query bit j being q_rot[j] > 0; (nq, min(k, n)) ids and scores,
+        score descending, ties by row ascending.  k <= 2048."""
+        rows = self._rows_of(compressed)
+        self._check_corpus(rows)
+        s, i = self._popcount(rows, self._rotate(queries, rows.device), k)
+        return topk_to_numpy(s, i)
+
+    def search_popcount(self, compressed, query, k: int = 10):
+        ids, sc = self.search_popcount_many(compressed, query, k=k)
+        return ids[0], sc[0]
+
+    def search_twostage_popcount_many(self, compressed, queries, k: int = 10,
+                                      candidates: int = 500):
+        """Two-stage search with the popcount coarse scorer: the top
+        `candidates` rows by sign agreement (ties by row), rescored at full
+        precision exactly as search_twostage's second stage
+        (remex/core.py:706-719); (nq, min(k, candidates, n)) results.
+        candidates <= 2048 unless it covers the whole corpus."""
+        rows = self._rows_of(compressed)
+        self._check_corpus(rows)
+        s, i = self._popcount(rows, self._rotate(queries, rows.device), k, candidates)
+        return topk_to_numpy(s, i)
+
+    def search_twostage_popcount(self, compressed, query, k: int = 10, candidates: int = 500):
+        ids, sc = self.search_twostage_popcount_many(compressed, query, k=k,
+                                                     candidates=candidates)
+        return ids[0], sc[0]
 
     def search_batch(self, compressed, queries, k: int = 10, precision: Optional[int] = None):
         """remex/core.py:721-778: (n_queries, min(k, n)) indices and scores."""

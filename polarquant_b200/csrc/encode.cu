@@ -34,6 +34,10 @@ constexpr int kEncBM = 128;     // rows per tile (TMEM lanes)
 constexpr int kEncBK = 64;      // K per stage: one 128-byte swizzle atom of fp16
 constexpr int kEncThreads = 320;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 epilogue
 constexpr int kScaleBias = 14;  // R planes hold R * 2^14
+constexpr int kGuideCells = 1024;  // uniform cells of the 8-bit guide table
+// Shared memory after the stages: barriers, TMEM address, abort flag, the
+// boundaries (255 f32) and the 8-bit guide table (kGuideCells + 1 bytes).
+constexpr size_t kEncMetaBytes = 4096;
 
 struct EncShape {
   int d, ntn, BN, ldn, ldk, nk, stages, tmem_cols;
@@ -54,7 +58,7 @@ static EncShape enc_shape(int d) {
   s.stages = (s.BN > 128) ? 2 : 3;
   s.tmem_cols = 32;
   while (s.tmem_cols < 2 * s.BN) s.tmem_cols <<= 1;
-  s.smem_bytes = 1024 + (size_t)s.stages * s.stage_bytes + 2048;
+  s.smem_bytes = 1024 + (size_t)s.stages * s.stage_bytes + kEncMetaBytes;
   return s;
 }
 
@@ -149,6 +153,47 @@ __device__ __forceinline__ uint32_t code_of(float x, const float* sb) {
   return idx;
 }
 
+// 8-bit codes: a guide table over kGuideCells uniform cells between the first
+// and last boundary gives each value a starting level (the number of
+// boundaries below its cell's left edge); a walk of one or two steps then
+// lands on #{boundaries < x} (searchsorted side='left').  The walk checks the
+// boundaries on both sides, so the result is exact whatever cell the float
+// arithmetic picks; the last line falls back to the binary search in the
+// (never observed) case that two steps were not enough.
+struct Guide {
+  float lo, scale;  // cell of x = (x - lo) * scale
+};
+
+__device__ __forceinline__ uint32_t code_guided(float x, const float* sb, const uint8_t* guide,
+                                                Guide g) {
+  constexpr uint32_t L1 = 255u;  // number of boundaries
+  float t = (x - g.lo) * g.scale;
+  t = fminf(fmaxf(t, 0.f), (float)(kGuideCells - 1));
+  uint32_t c = guide[(int)t];
+  // Up to two steps up, then one down; each compares against a boundary.
+  if (c < L1 && x > sb[c]) ++c;
+  if (c < L1 && x > sb[c]) ++c;
+  if (c > 0 && !(x > sb[c - 1])) --c;
+  const bool ok = (c == 0 || x > sb[c - 1]) && (c == L1 || !(x > sb[c]));
+  return ok ? c : code_of<8>(x, sb);
+}
+
+// Builds the guide table: guide[i] = #{boundaries < lo + i / scale}.
+__device__ __forceinline__ Guide build_guide(const float* sb, uint8_t* guide) {
+  Guide g;
+  g.lo = sb[0];
+  g.scale = (float)kGuideCells / (sb[254] - sb[0]);
+  for (int i = threadIdx.x; i <= kGuideCells; i += blockDim.x) {
+    const float e = g.lo + (float)i / g.scale;
+    uint32_t idx = 0;
+#pragma unroll
+    for (int step = 128; step > 0; step >>= 1)
+      if (e > sb[idx + step - 1]) idx += step;
+    guide[i] = (uint8_t)idx;
+  }
+  return g;
+}
+
 // Half-width of the band around each boundary inside which a coordinate is
 // recomputed exactly (rotated-coordinate units; the GEMM's own error is
 // ~1e-8, the reference's f32 sgemm error similar).
@@ -209,7 +254,8 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
                    const float* __restrict__ inv_scale, const float* __restrict__ bounds,
                    uint8_t* __restrict__ packed, int64_t ldb, int64_t rb, float* __restrict__ Y,
                    const __half* __restrict__ Ahi, const __half* __restrict__ Alo, int ldk,
-                   const float* __restrict__ R) {
+                   const float* __restrict__ R, unsigned long long* __restrict__ fix_list,
+                   unsigned int* __restrict__ fix_count, int fix_cap) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t raw = tc::smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -224,6 +270,7 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(gmeta + 8 * (2 * stages + 5));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gmeta + 8 * (2 * stages + 5) + 4);
   float* sb = reinterpret_cast<float*>(gmeta + 8 * (2 * stages + 5) + 8);
+  uint8_t* guide = gmeta + 8 * (2 * stages + 5) + 8 + 1024;  // 8-bit codes only
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -250,6 +297,11 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  Guide gd{0.f, 0.f};
+  if constexpr (BITS == 8) {
+    gd = build_guide(sb, guide);
+    __syncthreads();
+  }
 
   const int mt = (m + kEncBM - 1) / kEncBM;
   const int ntiles = mt * ntn;
@@ -361,8 +413,10 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
               if (col0 + i < d) yr[col0 + i] = __uint_as_float(v[i]) * inv;
           }
         } else {
-          // np.searchsorted(boundaries, x, side='left') for the 32 values,
-          // step-major so the 32 table lookups of a step are independent.
+          // np.searchsorted(boundaries, x, side='left') for the 32 values:
+          // 8-bit codes through the guide table, narrower ones by a binary
+          // search, step-major so the 32 table lookups of a step are
+          // independent.
           float x[32];
           uint32_t c[32];
 #pragma unroll
@@ -370,11 +424,16 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
             x[i] = __uint_as_float(v[i]) * inv;
             c[i] = 0;
           }
+          if constexpr (BITS == 8) {
 #pragma unroll
-          for (int step = 1 << (BITS - 1); step > 0; step >>= 1) {
+            for (int i = 0; i < 32; ++i) c[i] = code_guided(x[i], sb, guide, gd);
+          } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (x[i] > sb[c[i] + step - 1]) c[i] += step;
+            for (int step = 1 << (BITS - 1); step > 0; step >>= 1) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (x[i] > sb[c[i] + step - 1]) c[i] += step;
+            }
           }
           uint32_t near = 0;
 #pragma unroll
@@ -384,10 +443,31 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
             if (!valid) c[i] = 0;
             else if (near_boundary<BITS>(x[i], c[i], sb)) near |= 1u << i;
           }
-          // Coordinates within kFixBand of a boundary: the warp recomputes the
-          // dot product in f64 from the exact f32 R and the 22-bit x planes,
-          // so the side of the boundary does not depend on the tensor core's
-          // f32 accumulation order.
+          // Coordinates within kFixBand of a boundary are recomputed in f64
+          // from the exact f32 R and the 22-bit x planes, so the side of the
+          // boundary does not depend on the tensor core's f32 accumulation
+          // order.  They go to the fix-up list (encode_fix_kernel recomputes
+          // them all after this kernel, many warps at once, and patches the
+          // packed codes); only when the list is full does the warp
+          // recompute them here.
+          if (near && fix_list) {
+            const uint32_t cnt = (uint32_t)__popc(near);
+            const uint32_t base = atomicAdd(fix_count, cnt);
+            if (base + cnt <= (uint32_t)fix_cap) {
+              uint32_t msk = near, k = 0;
+              while (msk) {
+                const int i = __ffs(msk) - 1;
+                msk &= msk - 1;
+                fix_list[base + k++] =
+                    ((unsigned long long)row << 32) | (unsigned)(col0 + i);
+              }
+              near = 0;
+            } else {
+              // Slots reserved below the capacity stay unused: mark them.
+              for (uint32_t k = base; k < (uint32_t)fix_cap && k < base + cnt; ++k)
+                fix_list[k] = ~0ull;
+            }
+          }
           uint32_t pend = __ballot_sync(0xffffffffu, near != 0);
           while (pend) {
             const int src = __ffs(pend) - 1;
@@ -454,6 +534,72 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
   }
 }
 
+// Recomputes the coordinates the GEMM epilogue listed (within kFixBand of a
+// boundary) exactly as its inline path does -- f64 dot product of the 22-bit
+// x planes with the f32 R, scaled -- and writes their codes into the packed
+// rows.  One warp per entry; entries of one row may share a 32-bit word, so
+// each code is written with an atomic AND (clear its bits) and OR (set
+// them): codes occupy disjoint bits, so the order of the updates does not
+// matter.  Entries ~0 are slots reserved but left unused.
+template <int BITS>
+__global__ void __launch_bounds__(256)
+encode_fix_kernel(const unsigned long long* __restrict__ fix_list,
+                  const unsigned int* __restrict__ fix_count, int fix_cap,
+                  const __half* __restrict__ Ahi, const __half* __restrict__ Alo, int ldk,
+                  const float* __restrict__ inv_scale, const float* __restrict__ R, int d,
+                  const float* __restrict__ bounds, uint8_t* __restrict__ packed, int64_t ldb) {
+  __shared__ float sb[256];
+  for (int i = threadIdx.x; i < (1 << BITS) - 1; i += blockDim.x) sb[i] = bounds[i];
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const unsigned total = min(*fix_count, (unsigned)fix_cap);
+  const unsigned warps = gridDim.x * (blockDim.x >> 5);
+  for (unsigned e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); e < total; e += warps) {
+    const unsigned long long ent = fix_list[e];
+    if (ent == ~0ull) continue;  // warp-uniform
+    const int row = (int)(ent >> 32), col = (int)(ent & 0xFFFFFFFFu);
+    const __half* ah = Ahi + (int64_t)row * ldk;
+    const __half* al = Alo + (int64_t)row * ldk;
+    const float* rr = R + (int64_t)col * d;
+    double acc = 0.0;
+    for (int k = lane; k < d; k += 32)
+      acc = fma((double)(__half2float(ah[k]) + __half2float(al[k])), (double)__ldg(rr + k), acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane != 0) continue;
+    const float sinv = __ldg(inv_scale + row);
+    const float xr = (float)(acc * ((double)sinv * (double)(1 << kScaleBias)));
+    const uint32_t code = code_of<BITS>(xr, sb);
+    // Stream bit p + i (MSB-first) holds code bit BITS - 1 - i; at most two
+    // 32-bit words of the row are touched (3-bit codes may straddle bytes).
+    uint32_t* rowp = reinterpret_cast<uint32_t*>(packed + (int64_t)row * ldb);
+    const int p = col * BITS;
+    int w0 = -1, w1 = -1;
+    uint32_t m0 = 0, m1 = 0, v0 = 0, v1 = 0;
+#pragma unroll
+    for (int i = 0; i < BITS; ++i) {
+      const int bit = p + i, byte = bit >> 3;
+      const int sh = 8 * (byte & 3) + 7 - (bit & 7);
+      const uint32_t b = (code >> (BITS - 1 - i)) & 1u;
+      if (w0 < 0 || w0 == (byte >> 2)) {
+        w0 = byte >> 2;
+        m0 |= 1u << sh;
+        v0 |= b << sh;
+      } else {
+        w1 = byte >> 2;
+        m1 |= 1u << sh;
+        v1 |= b << sh;
+      }
+    }
+    atomicAnd(rowp + w0, ~m0);
+    atomicOr(rowp + w0, v0);
+    if (w1 >= 0) {
+      atomicAnd(rowp + w1, ~m1);
+      atomicOr(rowp + w1, v1);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -487,6 +633,14 @@ static int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int ldk, in
   return PQ_OK;
 }
 
+// Entries of the near-boundary fix-up list per chunk: ~2x the share of 8-bit
+// coordinates that land within kFixBand of a boundary (~0.2%); calls that
+// overflow it recompute the rest inline.
+static int enc_fix_cap(int64_t chunk_rows, int d) {
+  const int64_t c = chunk_rows * d / 256;
+  return (int)(c < 65536 ? 65536 : (c > (1 << 26) ? (1 << 26) : c));
+}
+
 // Rows per chunk (>= one M tile, so a TMA box never exceeds the tensor).
 static int64_t enc_chunk_rows(int64_t n) {
   const int64_t cap = 131072;
@@ -507,6 +661,9 @@ static int run_encode(const float* X, int64_t n, int d, const void* planes, cons
   __half* Ahi = cv.take<__half>((size_t)ch * s.ldk);
   __half* Alo = cv.take<__half>((size_t)ch * s.ldk);
   float* inv = cv.take<float>((size_t)ch);
+  const int fix_cap = enc_fix_cap(ch, d);
+  unsigned int* fix_count = cv.take<unsigned int>(1);
+  unsigned long long* fix_list = cv.take<unsigned long long>((size_t)fix_cap);
   if (!cv.ok()) return fail(PQ_ERR_WORKSPACE, "encode workspace too small (%zu bytes)", ws_bytes);
   const __half* Rhi = (const __half*)planes;
   const __half* Rlo = Rhi + (size_t)s.ldn * s.ldk;
@@ -534,6 +691,7 @@ static int run_encode(const float* X, int64_t n, int d, const void* planes, cons
     const int grid = ntiles < num_sms() ? ntiles : num_sms();
     uint8_t* pk = packed ? packed + r0 * ldb : nullptr;
     float* yk = Y ? Y + r0 * d : nullptr;
+    if (bits > 0) PQ_CUDA_TRY(cudaMemsetAsync(fix_count, 0, sizeof(unsigned int), st));
     switch (bits) {
 #define PQ_ENC_CASE(B)                                                                        \
   case B: {                                                                                   \
@@ -541,7 +699,14 @@ static int run_encode(const float* X, int64_t n, int d, const void* planes, cons
     PQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); \
     kern<<<grid, kEncThreads, sm, st>>>(mAhi, mAlo, mBhi, mBlo, (int)m, d, s.BN, s.ntn, s.nk,   \
                                         s.stages, s.tmem_cols, inv, bounds, pk, ldb, rb, yk,  \
-                                        Ahi, Alo, s.ldk, R);                                  \
+                                        Ahi, Alo, s.ldk, R, B > 0 ? fix_list : nullptr,       \
+                                        fix_count, fix_cap);                                  \
+    PQ_LAUNCH_CHECK("encode_gemm_kernel");                                                    \
+    if (B > 0) {                                                                              \
+      encode_fix_kernel<(B > 0 ? B : 1)><<<num_sms() * 4, 256, 0, st>>>(                       \
+          fix_list, fix_count, fix_cap, Ahi, Alo, s.ldk, inv, R, d, bounds, pk, ldb);          \
+      PQ_LAUNCH_CHECK("encode_fix_kernel");                                                   \
+    }                                                                                         \
   } break;
       PQ_ENC_CASE(0)
       PQ_ENC_CASE(1)
@@ -553,7 +718,6 @@ static int run_encode(const float* X, int64_t n, int d, const void* planes, cons
       default:
         return fail(PQ_ERR_INVALID, "bits must be one of 1,2,3,4,8 (got %d)", bits);
     }
-    PQ_LAUNCH_CHECK("encode_gemm_kernel");
   }
   return PQ_OK;
 }
@@ -586,7 +750,8 @@ size_t pq_encode_workspace_bytes(int64_t n, int d) {
   if (d <= 0) return 256;
   const EncShape s = enc_shape(d);
   const size_t ch = (size_t)enc_chunk_rows(n);
-  return align_up(ch * s.ldk * 2, 256) * 2 + align_up(ch * 4, 256) + 1024;
+  return align_up(ch * s.ldk * 2, 256) * 2 + align_up(ch * 4, 256) + 256 +
+         (size_t)enc_fix_cap((int64_t)ch, d) * 8 + 1024;
 }
 
 int pq_encode(const float* X, int64_t n, int d, const float* R, const void* planes,

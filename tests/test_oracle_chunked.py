@@ -58,3 +58,26 @@ def test_search_batch_cached_equals_search_batch():
     I2, S2 = O.search_batch_cached(R, Xh, nr, Q, k=20)
     np.testing.assert_array_equal(I1, I2)
     np.testing.assert_array_equal(S1, S2)
+
+
+def test_sign_scores_are_the_pm1_inner_product():
+    """The popcount score d - 2 * popcount(q_signs XOR row_signs) equals the
+    inner product of the +-1 sign vectors, and the 1-bit Matryoshka level
+    (the code's MSB) is the sign of the rotated coordinate."""
+    d, bits = 40, 4
+    R = haar_rotation(d, 42)
+    bnd, cent = lloyd_max_codebook(d, bits)
+    rng = np.random.default_rng(9)
+    X = rng.standard_normal((500, d)).astype(np.float32)
+    idx, _ = O.encode(X, R, bnd)
+    rot = O.rotated(X, R)
+    np.testing.assert_array_equal((idx >> (bits - 1)).astype(bool), rot > 0)
+    q = rng.standard_normal(d).astype(np.float32)
+    qr = O.exact_q_rot(R, q)
+    sq = np.where(qr > 0, 1, -1)
+    sr = np.where(idx >> (bits - 1), 1, -1)
+    np.testing.assert_array_equal(O.sign_scores(qr, idx, bits), sr @ sq)
+    ids, sc = O.search_popcount(R, bits, idx, q, k=50)
+    assert np.all(np.diff(sc) <= 0)
+    ties = np.diff(sc) == 0
+    assert np.all(np.diff(ids)[ties] > 0), "ties ordered by row"
