@@ -457,7 +457,8 @@ def encode_reference_line(args, cfg, torch, dev, world):
 def scan_kernel_name(rows, nq, k, p):
     from polarquant_b200 import _lib
     kind = _lib.query("pq_adc_scan_kernel", rows.n, rows.d, rows.bits, p, nq, k, rows.ldb)
-    return {2: "scan2_kernel (TMA-staged)", 1: "scan_topk_kernel", 3: "score_keys + sort"}.get(
+    return {4: "scan_bt_kernel (byte tables)", 2: "scan2_kernel (TMA-staged)",
+            1: "scan_topk_kernel", 3: "score_keys + sort"}.get(
         kind, "?")
 
 
@@ -583,7 +584,7 @@ def search_workload(args, cfg, torch, dist, dev, world, rank, steps, warmup, hea
     if args.quick:
         return {"metric": "queries/s", "value": qps, "ms_per_step": ms, "kernel_ms": kms,
                 "n_gpus": world, "quick": True, "encode_vectors_per_s": enc_vps * world,
-                "config": {"workload": cfg["name"]}}
+                "config": {"workload": cfg["name"], "corpus_rows": cfg["n"]}, "clocks": clocks}
 
     line = {
         "metric": "queries/s", "value": qps, "unit": "queries/s", "n_gpus": world,

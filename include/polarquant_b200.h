@@ -137,9 +137,14 @@ int pq_decode(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n,
  * Output: nq x k, ids are row + row_offset.
  * ------------------------------------------------------------------------- */
 size_t pq_adc_scan_workspace_bytes(int64_t n, int d, int nq, int k);
-/* Which kernel pq_adc_scan runs for this shape: 2 = TMA-staged streaming scan
- * (4- and 8-bit codes, n >= 256, ldb >= 128, table fits in shared memory),
- * 1 = generic streaming scan, 3 = full sort (k > PQ_TOPK_MAX).  Diagnostic. */
+/* Which kernel pq_adc_scan runs for this shape (with the workspace that
+ * pq_adc_scan_workspace_bytes gives): 4 = byte-table scan (1-, 2-, 4- and
+ * 8-bit codes, n >= 2^18, nq <= 64, k <= 512, ldb >= 128: one lookup per
+ * packed byte), 2 = TMA-staged streaming scan (4- and 8-bit codes, n >= 256,
+ * ldb >= 128, table fits in shared memory), 1 = generic streaming scan,
+ * 3 = full sort (k > PQ_TOPK_MAX).  Diagnostic.  A workspace smaller than
+ * pq_adc_scan_workspace_bytes but holding the candidate lists is accepted:
+ * the call then skips the byte-table scan. */
 int pq_adc_scan_kernel(int64_t n, int d, int bits, int precision, int nq, int k, int64_t ldb);
 int pq_adc_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
                 int bits, int precision, const float* qrot, int nq, const float* cent, int k,

@@ -59,6 +59,8 @@ struct BatArgs {
   long long row_offset;
   unsigned int* gthr;     // int8 kernel: per-query running threshold (ordered key, 0 = none)
   const int* qdig;        // int8 kernel: per query {sum |hi digit|, sum |lo digit|}
+  int out_parts;          // int8 kernel: lists per query in out_s / out_id
+  int part_base;          // int8 kernel: this launch's first list
 };
 
 // Loads the 8 codes k0..k0+7 (k0 % 8 == 0) of a row as the low bits of c[].
@@ -712,6 +714,7 @@ static int run_batched_1cta(const uint8_t* packed, int64_t ldb, const float* nor
   a.rows_per_chunk = b.rpc; a.K = K; a.cap = b.cap; a.qinv = w.qinv; a.cscale = w.cscale;
   a.lut = w.lut; a.lut_size = lut_size; a.buf_s = w.buf_s; a.buf_i = w.buf_i;
   a.out_s = w.out_s; a.out_id = w.out_id; a.row_offset = row_offset; a.gthr = nullptr; a.qdig = nullptr;
+  a.out_parts = b.rchunks; a.part_base = 0;
   if (b.smem > 227 * 1024) return fail(PQ_ERR_UNSUPPORTED, "batched smem %zu too large", b.smem);
   switch (bits) {
 #define PQ_BAT_CASE(BB)                                                                         \

@@ -618,6 +618,7 @@ static int run_batched(const uint8_t* packed, int64_t ldb, const float* norms, i
   a.rows_per_chunk = b.rpc; a.K = K; a.cap = b.cap; a.qinv = w.qinv; a.cscale = w.cscale;
   a.lut = w.lut; a.lut_size = lut_size; a.buf_s = w.buf_s; a.buf_i = w.buf_i;
   a.out_s = w.out_s; a.out_id = w.out_id; a.row_offset = row_offset; a.gthr = nullptr; a.qdig = nullptr;
+  a.out_parts = b.rchunks; a.part_base = 0;
   cudaLaunchConfig_t cfg;
   cudaLaunchAttribute at[1];
   pair_config(&cfg, at, b.grid, st);

@@ -644,7 +644,7 @@ pair_i8_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant_
             const int src = __ffs(pend) - 1;
             pend &= pend - 1;
             const int sq = qbase + 32 * quad + src;
-            const size_t o = ((size_t)sq * (2 * p.rchunks) + 2 * rc + half) * p.K;
+            const size_t o = ((size_t)sq * p.out_parts + p.part_base + 2 * rc + half) * p.K;
             warp_compact(src, lane, cnt, p.buf_s + buf_of(32 * quad + src),
                          p.buf_i + buf_of(32 * quad + src), p.K, ss, si, cnt, thr,
                          p.out_s + o, p.out_id + o, p.row_offset);
@@ -872,15 +872,57 @@ static I8Plan i8_plan(int64_t n, int d, int nq, int k, int slots, int bits) {
 
 struct I8Ws {
   int8_t *qhi, *qlo;
-  float *qscale, *cscale, *buf_s, *out_s;
+  float *qscale, *cscale, *buf_s, *out_s, *seed_s;
   uint32_t* lut;
   unsigned int* gthr;
   int* qdig;
   int* buf_i;
-  long long* out_id;
+  long long *out_id, *seed_id;
 };
 
-static size_t i8_ws_carve(const I8Plan& b, int nq, int K, void* ws, size_t ws_bytes, I8Ws* w) {
+// Rows of a first pass whose merged lists seed every query's threshold before
+// the rest of the corpus is scanned (0 = a single pass).  Without it each
+// task's threshold starts at -inf and rises only as the task's own rows (or
+// other tasks' of the same query) fill its list, so on shards of a few
+// million rows -- where a row chunk holds few rows close to a clustered
+// query -- most of the scan runs with a loose threshold and the epilogue
+// scores many groups row by row.  The K'-th best approximate score over the
+// first pass's rows is a lower bound of the K'-th best over all rows, so it
+// is a valid starting threshold.
+static int64_t i8_pilot_rows(int64_t n) {
+  if (n < ((int64_t)4 << 20)) return 0;
+  int64_t s = n / 8;
+  if (s < ((int64_t)1 << 20)) s = (int64_t)1 << 20;
+  if (s > ((int64_t)4 << 20)) s = (int64_t)4 << 20;
+  return s / kQN * kQN;
+}
+
+struct I8Run {
+  int npass, parts, grid_max;
+  int64_t first[2], rows[2];
+  I8Plan p[2];
+};
+
+static I8Run i8_run_plan(int64_t n, int d, int nq, int K, int slots, int bits) {
+  I8Run r;
+  const int64_t S = i8_pilot_rows(n);
+  r.npass = S > 0 ? 2 : 1;
+  r.first[0] = 0;
+  r.rows[0] = S > 0 ? S : n;
+  r.first[1] = S;
+  r.rows[1] = n - S;
+  r.parts = 0;
+  r.grid_max = 0;
+  for (int i = 0; i < r.npass; ++i) {
+    r.p[i] = i8_plan(r.rows[i], d, nq, K, slots, bits);
+    r.parts += 2 * r.p[i].rchunks;
+    if (r.p[i].grid > r.grid_max) r.grid_max = r.p[i].grid;
+  }
+  return r;
+}
+
+static size_t i8_ws_carve(const I8Run& r, int nq, int K, void* ws, size_t ws_bytes, I8Ws* w) {
+  const I8Plan& b = r.p[0];  // nq_pad, ldk and cap are the same for both passes
   Carve cv(ws, ws_bytes);
   w->qhi = cv.take<int8_t>((size_t)b.nq_pad * b.ldk);
   w->qlo = cv.take<int8_t>((size_t)b.nq_pad * b.ldk);
@@ -889,11 +931,22 @@ static size_t i8_ws_carve(const I8Plan& b, int nq, int K, void* ws, size_t ws_by
   w->lut = cv.take<uint32_t>(256 + 8);
   w->gthr = cv.take<unsigned int>((size_t)b.nq_pad);
   w->qdig = cv.take<int>((size_t)2 * b.nq_pad);
-  w->buf_s = cv.take<float>((size_t)b.grid * kQM * 2 * b.cap);
-  w->buf_i = cv.take<int>((size_t)b.grid * kQM * 2 * b.cap);
-  w->out_s = cv.take<float>((size_t)nq * 2 * b.rchunks * K);
-  w->out_id = cv.take<long long>((size_t)nq * 2 * b.rchunks * K);
+  w->buf_s = cv.take<float>((size_t)r.grid_max * kQM * 2 * b.cap);
+  w->buf_i = cv.take<int>((size_t)r.grid_max * kQM * 2 * b.cap);
+  w->out_s = cv.take<float>((size_t)nq * r.parts * K);
+  w->out_id = cv.take<long long>((size_t)nq * r.parts * K);
+  w->seed_s = r.npass > 1 ? cv.take<float>((size_t)nq * K) : nullptr;
+  w->seed_id = r.npass > 1 ? cv.take<long long>((size_t)nq * K) : nullptr;
   return cv.off + 256;
+}
+
+// gthr[q] = the K-th best of query q's merged first-pass lists (when it has K).
+__global__ void i8_seed_kernel(const float* __restrict__ s, const long long* __restrict__ id,
+                               int nq, int K, unsigned int* __restrict__ gthr) {
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  const size_t o = (size_t)q * K + K - 1;
+  if (id[o] >= 0) gthr[q] = ordered_key(s[o]);
 }
 
 // 2-D uint8 tensor map (rows x width bytes, row stride `stride`), box
@@ -919,23 +972,26 @@ static int make_map_u8(CUtensorMap* map, const void* ptr, int64_t rows, int64_t 
 
 using namespace pqb;
 
-// Runs the int8 pair kernel; leaves per-(query, row chunk) top-K lists in ws
-// (layout [nq][rchunks][K]) and returns their location.
+// Runs the int8 pair kernel (a threshold-seeding first pass and the main
+// pass on corpora of 4M+ rows, see i8_pilot_rows); leaves per-(query, row
+// chunk) top-K lists in ws (layout [nq][parts][K], ids local + row_offset) and
+// returns their location.
 static int run_batched_i8(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
                           int bits, int precision, const float* qrot, int nq, const float* cent,
                           int K, int64_t row_offset, void* ws, size_t ws_bytes, cudaStream_t st,
                           int slots, float** parts_s, long long** parts_id, int* nparts) {
-  const I8Plan b = i8_plan(n, d, nq, K, slots, bits);
+  const I8Run r = i8_run_plan(n, d, nq, K, slots, bits);
+  const I8Plan& b0 = r.p[0];
   I8Ws w;
-  const size_t need = i8_ws_carve(b, nq, K, ws, (size_t)-1 / 2, &w);
+  const size_t need = i8_ws_carve(r, nq, K, ws, (size_t)-1 / 2, &w);
   if (ws_bytes < need) return fail(PQ_ERR_WORKSPACE, "batched ADC needs %zu workspace bytes", need);
-  i8_ws_carve(b, nq, K, ws, ws_bytes, &w);
-  PQ_CUDA_TRY(cudaMemsetAsync(w.qhi, 0, (size_t)b.nq_pad * b.ldk, st));
-  PQ_CUDA_TRY(cudaMemsetAsync(w.qlo, 0, (size_t)b.nq_pad * b.ldk, st));
-  PQ_CUDA_TRY(cudaMemsetAsync(w.gthr, 0, (size_t)b.nq_pad * sizeof(unsigned int), st));
+  i8_ws_carve(r, nq, K, ws, ws_bytes, &w);
+  PQ_CUDA_TRY(cudaMemsetAsync(w.qhi, 0, (size_t)b0.nq_pad * b0.ldk, st));
+  PQ_CUDA_TRY(cudaMemsetAsync(w.qlo, 0, (size_t)b0.nq_pad * b0.ldk, st));
+  PQ_CUDA_TRY(cudaMemsetAsync(w.gthr, 0, (size_t)b0.nq_pad * sizeof(unsigned int), st));
   {
     const int pg = (nq + 7) / 8 < num_sms() * 16 ? (nq + 7) / 8 : num_sms() * 16;
-    qsplit_i8_kernel<<<pg, 256, 0, st>>>(qrot, nq, d, b.ldk, bits == 4 ? 1 : 0, w.qhi, w.qlo,
+    qsplit_i8_kernel<<<pg, 256, 0, st>>>(qrot, nq, d, b0.ldk, bits == 4 ? 1 : 0, w.qhi, w.qlo,
                                          w.qscale, w.qdig);
     PQ_LAUNCH_CHECK("qsplit_i8_kernel");
   }
@@ -943,22 +999,37 @@ static int run_batched_i8(const uint8_t* packed, int64_t ldb, const float* norms
   lut_i8_kernel<<<1, 256, 0, st>>>(cent, lut_size, bits == 4 ? bits - precision : 0, w.lut,
                                    w.cscale);
   PQ_LAUNCH_CHECK("lut_i8_kernel");
-  CUtensorMap mhi, mlo, mraw;
+  CUtensorMap mhi, mlo;
   int rc;
-  if ((rc = make_map_u8(&mhi, w.qhi, b.nq_pad, b.ldk, b.ldk, kQBK, kQM, true))) return rc;
-  if ((rc = make_map_u8(&mlo, w.qlo, b.nq_pad, b.ldk, b.ldk, kQBK, kQM, true))) return rc;
-  if ((rc = make_map_u8(&mraw, packed, n, ldb, ldb, kQBK * bits / 8, kQNh, false))) return rc;
-  BatArgs a;
-  a.packed = packed; a.ldb = ldb; a.norms = norms; a.n = n; a.d = d; a.nk = b.nk;
-  a.shift = bits - precision; a.nq = nq; a.qtiles = b.qtiles; a.rchunks = b.rchunks;
-  a.rows_per_chunk = b.rpc; a.K = K; a.cap = b.cap; a.qinv = w.qscale; a.cscale = w.cscale;
-  a.lut = w.lut; a.lut_size = lut_size; a.buf_s = w.buf_s; a.buf_i = w.buf_i;
-  a.out_s = w.out_s; a.out_id = w.out_id; a.row_offset = row_offset; a.gthr = w.gthr;
-  a.qdig = w.qdig;
-  cudaLaunchConfig_t cfg;
-  cudaLaunchAttribute at[1];
-  i8_config(&cfg, at, b.grid, b.smem, st);
-  switch (bits) {
+  if ((rc = make_map_u8(&mhi, w.qhi, b0.nq_pad, b0.ldk, b0.ldk, kQBK, kQM, true))) return rc;
+  if ((rc = make_map_u8(&mlo, w.qlo, b0.nq_pad, b0.ldk, b0.ldk, kQBK, kQM, true))) return rc;
+  int part_base = 0;
+  for (int pass = 0; pass < r.npass; ++pass) {
+    const I8Plan& b = r.p[pass];
+    const int64_t f = r.first[pass];
+    if (pass == 1) {
+      // Seed each query's threshold with the K-th best of the first pass.
+      rc = launch_merge(w.out_s, w.out_id, part_base, K, (long long)r.parts * K, K, nq, K, 0,
+                        w.seed_s, w.seed_id, st);
+      if (rc) return rc;
+      i8_seed_kernel<<<(nq + 255) / 256, 256, 0, st>>>(w.seed_s, w.seed_id, nq, K, w.gthr);
+      PQ_LAUNCH_CHECK("i8_seed_kernel");
+    }
+    CUtensorMap mraw;
+    if ((rc = make_map_u8(&mraw, packed + f * ldb, r.rows[pass], ldb, ldb, kQBK * bits / 8, kQNh,
+                          false)))
+      return rc;
+    BatArgs a;
+    a.packed = packed + f * ldb; a.ldb = ldb; a.norms = norms + f; a.n = r.rows[pass];
+    a.d = d; a.nk = b.nk; a.shift = bits - precision; a.nq = nq; a.qtiles = b.qtiles;
+    a.rchunks = b.rchunks; a.rows_per_chunk = b.rpc; a.K = K; a.cap = b.cap; a.qinv = w.qscale;
+    a.cscale = w.cscale; a.lut = w.lut; a.lut_size = lut_size; a.buf_s = w.buf_s;
+    a.buf_i = w.buf_i; a.out_s = w.out_s; a.out_id = w.out_id; a.row_offset = row_offset + f;
+    a.gthr = w.gthr; a.qdig = w.qdig; a.out_parts = r.parts; a.part_base = part_base;
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute at[1];
+    i8_config(&cfg, at, b.grid, b.smem, st);
+    switch (bits) {
 #define PQ_I8_CASE(BB)                                                                          \
   case BB: {                                                                                    \
     auto kern = pair_i8_kernel<BB>;                                                             \
@@ -966,18 +1037,20 @@ static int run_batched_i8(const uint8_t* packed, int64_t ldb, const float* norms
                                      (int)b.smem));                                             \
     PQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, mhi, mlo, mraw, a));                             \
   } break;
-    PQ_I8_CASE(2)
-    PQ_I8_CASE(4)
-    PQ_I8_CASE(8)
+      PQ_I8_CASE(2)
+      PQ_I8_CASE(4)
+      PQ_I8_CASE(8)
 #undef PQ_I8_CASE
-    default:
-      return fail(PQ_ERR_INVALID, "the int8 batched kernel takes 2-, 4- or 8-bit codes (got %d)",
-                  bits);
+      default:
+        return fail(PQ_ERR_INVALID,
+                    "the int8 batched kernel takes 2-, 4- or 8-bit codes (got %d)", bits);
+    }
+    PQ_LAUNCH_CHECK("pair_i8_kernel");
+    part_base += 2 * b.rchunks;
   }
-  PQ_LAUNCH_CHECK("pair_i8_kernel");
   *parts_s = w.out_s;
   *parts_id = w.out_id;
-  *nparts = 2 * b.rchunks;
+  *nparts = r.parts;
   return PQ_OK;
 }
 
@@ -985,7 +1058,7 @@ static size_t batched_i8_ws(int64_t n, int d, int nq, int k) {
   if (k + kI8Margin > kBatMaxK || n < kQN || d < kI8MinDim) return 256;
   const int slots = i8_slots();
   if (slots < 1) return 256;
-  const I8Plan b = i8_plan(n, d, nq, k + kI8Margin, slots, 4);
+  const I8Run r = i8_run_plan(n, d, nq, k + kI8Margin, slots, 4);
   I8Ws w;
-  return i8_ws_carve(b, nq, k + kI8Margin, nullptr, 0, &w);
+  return i8_ws_carve(r, nq, k + kI8Margin, nullptr, 0, &w);
 }

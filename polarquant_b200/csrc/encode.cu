@@ -26,6 +26,8 @@
 // floor (flips only occur within ~1e-7 of a boundary).
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 #include "tc.cuh"
 
 namespace pqb {
@@ -34,7 +36,8 @@ constexpr int kEncBM = 128;     // rows per tile (TMEM lanes)
 constexpr int kEncBK = 64;      // K per stage: one 128-byte swizzle atom of fp16
 constexpr int kEncThreads = 320;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 epilogue
 constexpr int kScaleBias = 14;  // R planes hold R * 2^14
-constexpr int kGuideCells = 1024;  // uniform cells of the 8-bit guide table
+constexpr int kGuideCells = 2048;  // uniform cells of the 8-bit guide table
+constexpr int kFixPerRow = 16;     // near-boundary columns listed per row for the fix-up
 // Shared memory after the stages: barriers, TMEM address, abort flag, the
 // boundaries (255 f32) and the 8-bit guide table (kGuideCells + 1 bytes).
 constexpr size_t kEncMetaBytes = 4096;
@@ -123,6 +126,86 @@ encode_prep_kernel(const float* __restrict__ X, int64_t m, int d, int ldk, __hal
   }
 }
 
+// The same, one warp per row with the whole row held in registers: T float4
+// per lane (T = ldk / 128 rounded up, ldk <= 2048), all loads issued before
+// the first use, so a few warps per SM keep enough bytes in flight to stream
+// at HBM rate while the encode GEMM of the previous chunk occupies the SMs.
+// Requires d % 4 == 0 and 16-byte aligned rows.  The f64 sum of squares runs
+// in another order than encode_prep_kernel's; both round to the same f32 norm
+// except in the rare case that an f64 sum lands within an ulp of an f32
+// rounding boundary (the tests check norms bit for bit).
+template <bool NORMALIZE, int T>
+__global__ void __launch_bounds__(128)
+encode_prep4_kernel(const float* __restrict__ X, int64_t m, int d, int ldk,
+                    __half* __restrict__ Ahi, __half* __restrict__ Alo,
+                    float* __restrict__ inv_scale, float* __restrict__ norms_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int nv = d >> 2, nk = ldk >> 2;
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < m;
+       r += warps) {
+    const float4* x4 = reinterpret_cast<const float4*>(X + r * d);
+    float4 v[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      const int i = lane + 32 * t;
+      v[t] = i < nv ? __ldg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    double ss = 0.0;
+    float mx = 0.f;
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      ss = fma((double)v[t].x, (double)v[t].x, ss);
+      ss = fma((double)v[t].y, (double)v[t].y, ss);
+      ss = fma((double)v[t].z, (double)v[t].z, ss);
+      ss = fma((double)v[t].w, (double)v[t].w, ss);
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[t].x), fabsf(v[t].y)), fmaxf(fabsf(v[t].z), fabsf(v[t].w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    const float nrm = __double2float_rn(__dsqrt_rn(ss));
+    const float den = fmaxf(nrm, 1e-8f);
+    if (NORMALIZE) mx = __fdiv_rn(mx, den);
+    int e = 0;
+    if (mx > 0.f) {
+      e = kScaleBias - ilogbf(mx);
+      e = max(-100, min(100, e));
+    }
+    const float sc = pow2f(e);
+    uint2* hp = reinterpret_cast<uint2*>(Ahi + r * ldk);
+    uint2* lp = reinterpret_cast<uint2*>(Alo + r * ldk);
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      const int i = lane + 32 * t;
+      if (i < nk) {
+        float a[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
+        __half h[4], l[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          float x = a[u];
+          if (NORMALIZE) x = __fdiv_rn(x, den);
+          x *= sc;
+          h[u] = __float2half_rn(x);
+          l[u] = __float2half_rn(x - __half2float(h[u]));
+        }
+        const __half2 h01 = __halves2half2(h[0], h[1]), h23 = __halves2half2(h[2], h[3]);
+        const __half2 l01 = __halves2half2(l[0], l[1]), l23 = __halves2half2(l[2], l[3]);
+        hp[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&h01),
+                           *reinterpret_cast<const uint32_t*>(&h23));
+        lp[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&l01),
+                           *reinterpret_cast<const uint32_t*>(&l23));
+      }
+    }
+    if (lane == 0) {
+      inv_scale[r] = pow2f(-e - kScaleBias);
+      if (norms_out) norms_out[r] = nrm;
+    }
+  }
+}
+
 // R (d x d f32) -> R*2^14 split into fp16 hi/lo planes of ldn x ldk, zero padded.
 __global__ void rot_planes_kernel(const float* __restrict__ R, int d, int ldn, int ldk,
                                   __half* __restrict__ Rhi, __half* __restrict__ Rlo) {
@@ -154,28 +237,21 @@ __device__ __forceinline__ uint32_t code_of(float x, const float* sb) {
 }
 
 // 8-bit codes: a guide table over kGuideCells uniform cells between the first
-// and last boundary gives each value a starting level (the number of
-// boundaries below its cell's left edge); a walk of one or two steps then
-// lands on #{boundaries < x} (searchsorted side='left').  The walk checks the
-// boundaries on both sides, so the result is exact whatever cell the float
-// arithmetic picks; the last line falls back to the binary search in the
-// (never observed) case that two steps were not enough.
+// and last boundary gives each value a starting level -- the number of
+// boundaries below its cell's left edge.  Cells are narrower than the
+// smallest gap between boundaries, so a cell holds at most one and a single
+// step up (x > sb[c]) lands on #{boundaries < x} (searchsorted side='left').
+// The epilogue then checks the boundaries on both sides (which also gives
+// the near-boundary test) and sends any value that fails -- float rounding
+// of the cell index, NaN -- to the binary search.
 struct Guide {
   float lo, scale;  // cell of x = (x - lo) * scale
 };
 
-__device__ __forceinline__ uint32_t code_guided(float x, const float* sb, const uint8_t* guide,
-                                                Guide g) {
-  constexpr uint32_t L1 = 255u;  // number of boundaries
+__device__ __forceinline__ uint32_t guide_start(float x, const uint8_t* guide, Guide g) {
   float t = (x - g.lo) * g.scale;
   t = fminf(fmaxf(t, 0.f), (float)(kGuideCells - 1));
-  uint32_t c = guide[(int)t];
-  // Up to two steps up, then one down; each compares against a boundary.
-  if (c < L1 && x > sb[c]) ++c;
-  if (c < L1 && x > sb[c]) ++c;
-  if (c > 0 && !(x > sb[c - 1])) --c;
-  const bool ok = (c == 0 || x > sb[c - 1]) && (c == L1 || !(x > sb[c]));
-  return ok ? c : code_of<8>(x, sb);
+  return guide[(int)t];
 }
 
 // Builds the guide table: guide[i] = #{boundaries < lo + i / scale}.
@@ -254,8 +330,8 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
                    const float* __restrict__ inv_scale, const float* __restrict__ bounds,
                    uint8_t* __restrict__ packed, int64_t ldb, int64_t rb, float* __restrict__ Y,
                    const __half* __restrict__ Ahi, const __half* __restrict__ Alo, int ldk,
-                   const float* __restrict__ R, unsigned long long* __restrict__ fix_list,
-                   unsigned int* __restrict__ fix_count, int fix_cap) {
+                   const float* __restrict__ R, int* __restrict__ fix_cnt,
+                   uint16_t* __restrict__ fix_cols) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t raw = tc::smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -424,9 +500,25 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
             x[i] = __uint_as_float(v[i]) * inv;
             c[i] = 0;
           }
+          uint32_t near8 = 0, bad8 = 0;
           if constexpr (BITS == 8) {
+            // Step-major: each round's 32 lookups are independent.
 #pragma unroll
-            for (int i = 0; i < 32; ++i) c[i] = code_guided(x[i], sb, guide, gd);
+            for (int i = 0; i < 32; ++i) c[i] = guide_start(x[i], guide, gd);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) c[i] += (c[i] < 255u && x[i] > sb[c[i]]) ? 1u : 0u;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float lo = c[i] > 0u ? sb[c[i] - 1u] : -INFINITY;
+              const float hi = c[i] < 255u ? sb[c[i]] : INFINITY;
+              if (!(x[i] > lo) || x[i] > hi) bad8 |= 1u << i;
+              if (x[i] - lo < kFixBand || hi - x[i] < kFixBand) near8 |= 1u << i;
+            }
+            if (__any_sync(0xffffffffu, bad8 != 0u)) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if ((bad8 >> i) & 1u) c[i] = code_of<8>(x[i], sb);
+            }
           } else {
 #pragma unroll
             for (int step = 1 << (BITS - 1); step > 0; step >>= 1) {
@@ -440,33 +532,31 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
           for (int i = 0; i < 32; ++i) {
             if (isnan(x[i])) c[i] = (1u << BITS) - 1u;  // NaN sorts last, as in NumPy
             const bool valid = rv && col0 + i < d;
-            if (!valid) c[i] = 0;
-            else if (near_boundary<BITS>(x[i], c[i], sb)) near |= 1u << i;
+            if (!valid) {
+              c[i] = 0;
+            } else if (BITS == 8 && !((bad8 >> i) & 1u)) {
+              if ((near8 >> i) & 1u) near |= 1u << i;
+            } else if (near_boundary<BITS>(x[i], c[i], sb)) {
+              near |= 1u << i;
+            }
           }
           // Coordinates within kFixBand of a boundary are recomputed in f64
           // from the exact f32 R and the 22-bit x planes, so the side of the
           // boundary does not depend on the tensor core's f32 accumulation
-          // order.  They go to the fix-up list (encode_fix_kernel recomputes
-          // them all after this kernel, many warps at once, and patches the
-          // packed codes); only when the list is full does the warp
-          // recompute them here.
-          if (near && fix_list) {
-            const uint32_t cnt = (uint32_t)__popc(near);
-            const uint32_t base = atomicAdd(fix_count, cnt);
-            if (base + cnt <= (uint32_t)fix_cap) {
-              uint32_t msk = near, k = 0;
-              while (msk) {
-                const int i = __ffs(msk) - 1;
-                msk &= msk - 1;
-                fix_list[base + k++] =
-                    ((unsigned long long)row << 32) | (unsigned)(col0 + i);
-              }
-              near = 0;
-            } else {
-              // Slots reserved below the capacity stay unused: mark them.
-              for (uint32_t k = base; k < (uint32_t)fix_cap && k < base + cnt; ++k)
-                fix_list[k] = ~0ull;
+          // order.  They go to the row's fix-up list (encode_fix_kernel
+          // recomputes all listed coordinates after this kernel, a warp per
+          // row, and patches the packed codes); only coordinates past the
+          // list's kFixPerRow slots are recomputed here.
+          if (near && fix_cnt) {
+            const int cnt = __popc(near);
+            const int base = atomicAdd(fix_cnt + row, cnt);
+            uint32_t msk = near;
+            for (int k = base; msk && k < kFixPerRow; ++k) {
+              const int i = __ffs(msk) - 1;
+              msk &= msk - 1;
+              fix_cols[(size_t)row * kFixPerRow + k] = (uint16_t)(col0 + i);
             }
+            near = msk;
           }
           uint32_t pend = __ballot_sync(0xffffffffu, near != 0);
           while (pend) {
@@ -537,65 +627,107 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
 // Recomputes the coordinates the GEMM epilogue listed (within kFixBand of a
 // boundary) exactly as its inline path does -- f64 dot product of the 22-bit
 // x planes with the f32 R, scaled -- and writes their codes into the packed
-// rows.  One warp per entry; entries of one row may share a 32-bit word, so
+// rows.  One warp per row with listed columns: the row's x (hi + lo, exact
+// in f32, read with 16-byte loads and kept in L1 across the row's entries) is
+// dotted with each listed column of R.  One 128-thread block per SM fits
+// beside the encode GEMM.  A row's codes may share a 32-bit word, so
 // each code is written with an atomic AND (clear its bits) and OR (set
 // them): codes occupy disjoint bits, so the order of the updates does not
-// matter.  Entries ~0 are slots reserved but left unused.
+// matter.
 template <int BITS>
-__global__ void __launch_bounds__(256)
-encode_fix_kernel(const unsigned long long* __restrict__ fix_list,
-                  const unsigned int* __restrict__ fix_count, int fix_cap,
-                  const __half* __restrict__ Ahi, const __half* __restrict__ Alo, int ldk,
-                  const float* __restrict__ inv_scale, const float* __restrict__ R, int d,
-                  const float* __restrict__ bounds, uint8_t* __restrict__ packed, int64_t ldb) {
+__global__ void __launch_bounds__(128)
+encode_fix_kernel(const int* __restrict__ fix_cnt, const uint16_t* __restrict__ fix_cols,
+                  int64_t m, const __half* __restrict__ Ahi, const __half* __restrict__ Alo,
+                  int ldk, const float* __restrict__ inv_scale, const float* __restrict__ R,
+                  int d, const float* __restrict__ bounds, uint8_t* __restrict__ packed,
+                  int64_t ldb) {
   __shared__ float sb[256];
   for (int i = threadIdx.x; i < (1 << BITS) - 1; i += blockDim.x) sb[i] = bounds[i];
   __syncthreads();
   const int lane = threadIdx.x & 31;
-  const unsigned total = min(*fix_count, (unsigned)fix_cap);
-  const unsigned warps = gridDim.x * (blockDim.x >> 5);
-  for (unsigned e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); e < total; e += warps) {
-    const unsigned long long ent = fix_list[e];
-    if (ent == ~0ull) continue;  // warp-uniform
-    const int row = (int)(ent >> 32), col = (int)(ent & 0xFFFFFFFFu);
-    const __half* ah = Ahi + (int64_t)row * ldk;
-    const __half* al = Alo + (int64_t)row * ldk;
-    const float* rr = R + (int64_t)col * d;
-    double acc = 0.0;
-    for (int k = lane; k < d; k += 32)
-      acc = fma((double)(__half2float(ah[k]) + __half2float(al[k])), (double)__ldg(rr + k), acc);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane != 0) continue;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); row < m;
+       row += warps) {
+    const int cnt = min(__ldg(fix_cnt + row), kFixPerRow);
+    if (cnt == 0) continue;  // warp-uniform
+    // 16-byte loads: 8 consecutive elements per lane and step (the row's
+    // planes stay in L1 across its listed columns).
+    const uint4* ah = reinterpret_cast<const uint4*>(Ahi + row * ldk);
+    const uint4* al = reinterpret_cast<const uint4*>(Alo + row * ldk);
     const float sinv = __ldg(inv_scale + row);
-    const float xr = (float)(acc * ((double)sinv * (double)(1 << kScaleBias)));
-    const uint32_t code = code_of<BITS>(xr, sb);
-    // Stream bit p + i (MSB-first) holds code bit BITS - 1 - i; at most two
-    // 32-bit words of the row are touched (3-bit codes may straddle bytes).
-    uint32_t* rowp = reinterpret_cast<uint32_t*>(packed + (int64_t)row * ldb);
-    const int p = col * BITS;
-    int w0 = -1, w1 = -1;
-    uint32_t m0 = 0, m1 = 0, v0 = 0, v1 = 0;
+    uint32_t* rowp = reinterpret_cast<uint32_t*>(packed + row * ldb);
+    for (int k = 0; k < cnt; ++k) {
+      const int col = fix_cols[(size_t)row * kFixPerRow + k];
+      const float* rr = R + (int64_t)col * d;
+      // Two steps' loads (512 columns of the warp) are in flight before the
+      // first FMA of the pair.
+      double acc = 0.0;
+      for (int c0 = 0; 8 * c0 < d; c0 += 64) {
+        uint4 hv[2], lv[2];
+        float4 ra[2], rb[2];
 #pragma unroll
-    for (int i = 0; i < BITS; ++i) {
-      const int bit = p + i, byte = bit >> 3;
-      const int sh = 8 * (byte & 3) + 7 - (bit & 7);
-      const uint32_t b = (code >> (BITS - 1 - i)) & 1u;
-      if (w0 < 0 || w0 == (byte >> 2)) {
-        w0 = byte >> 2;
-        m0 |= 1u << sh;
-        v0 |= b << sh;
-      } else {
-        w1 = byte >> 2;
-        m1 |= 1u << sh;
-        v1 |= b << sh;
+        for (int t = 0; t < 2; ++t) {
+          const int c8 = c0 + lane + 32 * t;
+          if (8 * c8 < d) {
+            hv[t] = __ldg(ah + c8);
+            lv[t] = __ldg(al + c8);
+            if (8 * c8 + 8 <= d) {
+              ra[t] = __ldg(reinterpret_cast<const float4*>(rr) + 2 * c8);
+              rb[t] = __ldg(reinterpret_cast<const float4*>(rr) + 2 * c8 + 1);
+            } else {
+              float tmp[8];
+#pragma unroll
+              for (int u = 0; u < 8; ++u) tmp[u] = 8 * c8 + u < d ? __ldg(rr + 8 * c8 + u) : 0.f;
+              ra[t] = make_float4(tmp[0], tmp[1], tmp[2], tmp[3]);
+              rb[t] = make_float4(tmp[4], tmp[5], tmp[6], tmp[7]);
+            }
+          } else {
+            hv[t] = lv[t] = make_uint4(0, 0, 0, 0);
+            ra[t] = rb[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const __half* hh = reinterpret_cast<const __half*>(&hv[t]);
+          const __half* ll = reinterpret_cast<const __half*>(&lv[t]);
+          const float r8[8] = {ra[t].x, ra[t].y, ra[t].z, ra[t].w,
+                               rb[t].x, rb[t].y, rb[t].z, rb[t].w};
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            acc = fma((double)(__half2float(hh[u]) + __half2float(ll[u])), (double)r8[u], acc);
+        }
       }
-    }
-    atomicAnd(rowp + w0, ~m0);
-    atomicOr(rowp + w0, v0);
-    if (w1 >= 0) {
-      atomicAnd(rowp + w1, ~m1);
-      atomicOr(rowp + w1, v1);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane != 0) continue;
+      const float xr = (float)(acc * ((double)sinv * (double)(1 << kScaleBias)));
+      const uint32_t code = code_of<BITS>(xr, sb);
+      // Stream bit p + i (MSB-first) holds code bit BITS - 1 - i; at most two
+      // 32-bit words of the row are touched (3-bit codes may straddle bytes).
+      const int p = col * BITS;
+      int w0 = -1, w1 = -1;
+      uint32_t m0 = 0, m1 = 0, v0 = 0, v1 = 0;
+#pragma unroll
+      for (int i = 0; i < BITS; ++i) {
+        const int bit = p + i, byte = bit >> 3;
+        const int sh = 8 * (byte & 3) + 7 - (bit & 7);
+        const uint32_t b = (code >> (BITS - 1 - i)) & 1u;
+        if (w0 < 0 || w0 == (byte >> 2)) {
+          w0 = byte >> 2;
+          m0 |= 1u << sh;
+          v0 |= b << sh;
+        } else {
+          w1 = byte >> 2;
+          m1 |= 1u << sh;
+          v1 |= b << sh;
+        }
+      }
+      atomicAnd(rowp + w0, ~m0);
+      atomicOr(rowp + w0, v0);
+      if (w1 >= 0) {
+        atomicAnd(rowp + w1, ~m1);
+        atomicOr(rowp + w1, v1);
+      }
     }
   }
 }
@@ -633,14 +765,6 @@ static int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int ldk, in
   return PQ_OK;
 }
 
-// Entries of the near-boundary fix-up list per chunk: ~2x the share of 8-bit
-// coordinates that land within kFixBand of a boundary (~0.2%); calls that
-// overflow it recompute the rest inline.
-static int enc_fix_cap(int64_t chunk_rows, int d) {
-  const int64_t c = chunk_rows * d / 256;
-  return (int)(c < 65536 ? 65536 : (c > (1 << 26) ? (1 << 26) : c));
-}
-
 // Rows per chunk (>= one M tile, so a TMA box never exceeds the tensor).
 static int64_t enc_chunk_rows(int64_t n) {
   const int64_t cap = 131072;
@@ -652,61 +776,201 @@ static int64_t enc_chunk_rows(int64_t n) {
 
 using namespace pqb;
 
+// Per device: the side stream and events of the encode pipeline (created on
+// first use; the pipeline's enqueue runs under a mutex, so concurrent encode
+// calls from several host threads do not interleave their event records).
+struct EncSide {
+  cudaStream_t s2;
+  cudaEvent_t start, prep[2], gemm[2], end;
+  bool ok;
+};
+static EncSide g_enc_side[64];
+static std::mutex g_enc_mu;
+
+static int enc_side(EncSide** out) {
+  int dev = 0;
+  PQ_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(PQ_ERR_CUDA, "device ordinal %d out of range", dev);
+  EncSide& e = g_enc_side[dev];
+  if (!e.ok) {
+    PQ_CUDA_TRY(cudaStreamCreateWithFlags(&e.s2, cudaStreamNonBlocking));
+    PQ_CUDA_TRY(cudaEventCreateWithFlags(&e.start, cudaEventDisableTiming));
+    PQ_CUDA_TRY(cudaEventCreateWithFlags(&e.end, cudaEventDisableTiming));
+    for (int i = 0; i < 2; ++i) {
+      PQ_CUDA_TRY(cudaEventCreateWithFlags(&e.prep[i], cudaEventDisableTiming));
+      PQ_CUDA_TRY(cudaEventCreateWithFlags(&e.gemm[i], cudaEventDisableTiming));
+    }
+    e.ok = true;
+  }
+  *out = &e;
+  return PQ_OK;
+}
+
+// Kernels that run beside the encode GEMM (which keeps ~200 KB of shared
+// memory per SM) ask for the same maximal shared-memory carveout: an SM runs
+// blocks of different kernels at once only under one L1 / shared-memory
+// split, so with the default preference their blocks would wait for the GEMM
+// to leave the SM.
+static void enc_side_carveout(const void* kern) {
+  cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                       (int)cudaSharedmemCarveoutMaxShared);
+}
+
+// side: the prep runs beside an encode GEMM, so one 128-thread block per SM
+// (more blocks could take the shared memory the GEMM's next CTA needs).
+static int launch_prep(const float* X, int64_t m, int d, int ldk, __half* Ahi, __half* Alo,
+                       float* inv, float* norms, bool normalize, bool side, cudaStream_t st) {
+  const int T = (ldk + 127) / 128;
+  if (d % 4 == 0 && ((uintptr_t)X & 15) == 0 && T <= 16) {
+    int g = (int)((m + 3) / 4);
+    const int gmax = side ? num_sms() : num_sms() * 32;
+    if (g > gmax) g = gmax;
+    switch (T) {
+#define PQ_PREP4(TT)                                                                         \
+  case TT:                                                                                   \
+    if (normalize) {                                                                         \
+      enc_side_carveout((const void*)encode_prep4_kernel<true, TT>);                         \
+      encode_prep4_kernel<true, TT><<<g, 128, 0, st>>>(X, m, d, ldk, Ahi, Alo, inv, norms);  \
+    } else {                                                                                 \
+      enc_side_carveout((const void*)encode_prep4_kernel<false, TT>);                        \
+      encode_prep4_kernel<false, TT><<<g, 128, 0, st>>>(X, m, d, ldk, Ahi, Alo, inv, norms); \
+    }                                                                                        \
+    break;
+      PQ_PREP4(1) PQ_PREP4(2) PQ_PREP4(3) PQ_PREP4(4) PQ_PREP4(5) PQ_PREP4(6) PQ_PREP4(7)
+      PQ_PREP4(8) PQ_PREP4(9) PQ_PREP4(10) PQ_PREP4(11) PQ_PREP4(12) PQ_PREP4(13)
+      PQ_PREP4(14) PQ_PREP4(15) PQ_PREP4(16)
+#undef PQ_PREP4
+    }
+    PQ_LAUNCH_CHECK("encode_prep4_kernel");
+    return PQ_OK;
+  }
+  const int pg = (int)((m + 7) / 8 < (int64_t)num_sms() * 16 ? (m + 7) / 8 : num_sms() * 16);
+  if (normalize)
+    encode_prep_kernel<true><<<pg, 256, 0, st>>>(X, m, d, ldk, Ahi, Alo, inv, norms);
+  else
+    encode_prep_kernel<false><<<pg, 256, 0, st>>>(X, m, d, ldk, Ahi, Alo, inv, norms);
+  PQ_LAUNCH_CHECK("encode_prep_kernel");
+  return PQ_OK;
+}
+
+// Plane buffers of a call: two (ping-pong) when it spans several chunks.
+static int enc_buffers(int64_t n) { return n > enc_chunk_rows(n) ? 2 : 1; }
+
+// Encode in row chunks.  With several chunks the work runs as a pipeline on
+// the caller's stream `st` and a side stream s2, ordered by events only (no
+// host synchronisation):
+//   s2: prep(0) prep(1) | fix(0) prep(2) | fix(1) prep(3) | ...
+//   st:                 | gemm(0)        | gemm(1)        | ...
+// so the HBM-bound normalise/split of chunk i+1 and the f64 fix-ups of chunk
+// i-1 run while the tensor-bound GEMM of chunk i occupies the SMs.  Chunk i
+// uses plane buffer i % 2; prep(i + 2) is enqueued on s2 after fix(i), which
+// waits for gemm(i): the buffer is free by then.  `st` waits for s2's last
+// work before the call returns its work to the caller.
 static int run_encode(const float* X, int64_t n, int d, const void* planes, const float* R,
                       const float* bounds, int bits, uint8_t* packed, int64_t ldb, float* norms,
                       float* Y, void* ws, size_t ws_bytes, cudaStream_t st) {
   const EncShape s = enc_shape(d);
   const int64_t ch = enc_chunk_rows(n);
+  const int nbuf = enc_buffers(n);
   Carve cv(ws, ws_bytes);
-  __half* Ahi = cv.take<__half>((size_t)ch * s.ldk);
-  __half* Alo = cv.take<__half>((size_t)ch * s.ldk);
-  float* inv = cv.take<float>((size_t)ch);
-  const int fix_cap = enc_fix_cap(ch, d);
-  unsigned int* fix_count = cv.take<unsigned int>(1);
-  unsigned long long* fix_list = cv.take<unsigned long long>((size_t)fix_cap);
+  __half *Ahi[2], *Alo[2];
+  float* inv[2];
+  int* fix_cnt[2];
+  uint16_t* fix_cols[2];
+  // The listed fix-ups need d <= 2048 (the fix kernel keeps the row in
+  // registers; columns fit 16 bits); wider rows recompute inline.
+  const bool deferred = bits > 0 && d <= 2048;
+  for (int b = 0; b < nbuf; ++b) {
+    Ahi[b] = cv.take<__half>((size_t)ch * s.ldk);
+    Alo[b] = cv.take<__half>((size_t)ch * s.ldk);
+    inv[b] = cv.take<float>((size_t)ch);
+    fix_cnt[b] = cv.take<int>((size_t)ch);
+    fix_cols[b] = cv.take<uint16_t>((size_t)ch * kFixPerRow);
+  }
   if (!cv.ok()) return fail(PQ_ERR_WORKSPACE, "encode workspace too small (%zu bytes)", ws_bytes);
   const __half* Rhi = (const __half*)planes;
   const __half* Rlo = Rhi + (size_t)s.ldn * s.ldk;
-  CUtensorMap mAhi, mAlo, mBhi, mBlo;
+  CUtensorMap mAhi[2], mAlo[2], mBhi, mBlo;
   int rc;
-  if ((rc = make_map(&mAhi, Ahi, ch, s.ldk, kEncBM))) return rc;
-  if ((rc = make_map(&mAlo, Alo, ch, s.ldk, kEncBM))) return rc;
+  for (int b = 0; b < nbuf; ++b) {
+    if ((rc = make_map(&mAhi[b], Ahi[b], ch, s.ldk, kEncBM))) return rc;
+    if ((rc = make_map(&mAlo[b], Alo[b], ch, s.ldk, kEncBM))) return rc;
+  }
   if ((rc = make_map(&mBhi, Rhi, s.ldn, s.ldk, s.BN))) return rc;
   if ((rc = make_map(&mBlo, Rlo, s.ldn, s.ldk, s.BN))) return rc;
 
   const size_t sm = s.smem_bytes;
   if (sm > 227 * 1024) return fail(PQ_ERR_UNSUPPORTED, "encode tile needs %zu bytes of smem", sm);
   const int64_t rb = row_bytes(d, bits > 0 ? bits : 8);
-  for (int64_t r0 = 0; r0 < n; r0 += ch) {
-    const int64_t m = (n - r0 < ch) ? n - r0 : ch;
-    const int pg = (int)((m + 7) / 8 < (int64_t)num_sms() * 16 ? (m + 7) / 8 : num_sms() * 16);
-    if (bits > 0)
-      encode_prep_kernel<true><<<pg, 256, 0, st>>>(X + r0 * d, m, d, s.ldk, Ahi, Alo, inv,
-                                                   norms ? norms + r0 : nullptr);
-    else
-      encode_prep_kernel<false><<<pg, 256, 0, st>>>(X + r0 * d, m, d, s.ldk, Ahi, Alo, inv,
-                                                    nullptr);
-    PQ_LAUNCH_CHECK("encode_prep_kernel");
+  const int nch = (int)((n + ch - 1) / ch);
+
+  std::unique_lock<std::mutex> lock(g_enc_mu, std::defer_lock);
+  EncSide* side = nullptr;
+  cudaStream_t s2 = st;  // one chunk: everything on the caller's stream
+  if (nbuf == 2) {
+    lock.lock();
+    if ((rc = enc_side(&side))) return rc;
+    s2 = side->s2;
+    PQ_CUDA_TRY(cudaEventRecord(side->start, st));
+    PQ_CUDA_TRY(cudaStreamWaitEvent(s2, side->start, 0));
+  }
+  auto chunk_rows = [&](int i) { return (n - (int64_t)i * ch < ch) ? n - (int64_t)i * ch : ch; };
+  auto prep = [&](int i) -> int {
+    const int b = i % nbuf;
+    const int64_t r0 = (int64_t)i * ch;
+    int r = launch_prep(X + r0 * d, chunk_rows(i), d, s.ldk, Ahi[b], Alo[b], inv[b],
+                        (bits > 0 && norms) ? norms + r0 : nullptr, bits > 0, i > 0, s2);
+    if (r) return r;
+    if (side) PQ_CUDA_TRY(cudaEventRecord(side->prep[b], s2));
+    return PQ_OK;
+  };
+  auto fix = [&](int i) -> int {
+    if (!deferred) return PQ_OK;
+    const int b = i % nbuf;
+    const int64_t r0 = (int64_t)i * ch;
+    const int64_t m = chunk_rows(i);
+    uint8_t* pk = packed + r0 * ldb;
+    // One block per SM when it runs beside the next chunk's GEMM.
+    const int g = nbuf == 2 ? num_sms() : num_sms() * 16;
+    switch (bits) {
+#define PQ_FIX_CASE(B)                                                                      \
+  case B:                                                                                   \
+    enc_side_carveout((const void*)encode_fix_kernel<B>);                                   \
+    encode_fix_kernel<B><<<g, 128, 0, s2>>>(fix_cnt[b], fix_cols[b], m, Ahi[b], Alo[b],     \
+                                            s.ldk, inv[b], R, d, bounds, pk, ldb);          \
+    break;
+      PQ_FIX_CASE(1)
+      PQ_FIX_CASE(2)
+      PQ_FIX_CASE(3)
+      PQ_FIX_CASE(4)
+      PQ_FIX_CASE(8)
+#undef PQ_FIX_CASE
+    }
+    PQ_LAUNCH_CHECK("encode_fix_kernel");
+    return PQ_OK;
+  };
+
+  if ((rc = prep(0))) return rc;
+  if (nch > 1 && (rc = prep(1))) return rc;
+  for (int i = 0; i < nch; ++i) {
+    const int b = i % nbuf;
+    const int64_t r0 = (int64_t)i * ch;
+    const int64_t m = chunk_rows(i);
+    if (side) PQ_CUDA_TRY(cudaStreamWaitEvent(st, side->prep[b], 0));
     const int ntiles = (int)((m + kEncBM - 1) / kEncBM) * s.ntn;
     const int grid = ntiles < num_sms() ? ntiles : num_sms();
     uint8_t* pk = packed ? packed + r0 * ldb : nullptr;
     float* yk = Y ? Y + r0 * d : nullptr;
-    if (bits > 0) PQ_CUDA_TRY(cudaMemsetAsync(fix_count, 0, sizeof(unsigned int), st));
+    if (deferred) PQ_CUDA_TRY(cudaMemsetAsync(fix_cnt[b], 0, sizeof(int) * (size_t)m, st));
     switch (bits) {
 #define PQ_ENC_CASE(B)                                                                        \
   case B: {                                                                                   \
     auto kern = encode_gemm_kernel<B>;                                                        \
     PQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); \
-    kern<<<grid, kEncThreads, sm, st>>>(mAhi, mAlo, mBhi, mBlo, (int)m, d, s.BN, s.ntn, s.nk,   \
-                                        s.stages, s.tmem_cols, inv, bounds, pk, ldb, rb, yk,  \
-                                        Ahi, Alo, s.ldk, R, B > 0 ? fix_list : nullptr,       \
-                                        fix_count, fix_cap);                                  \
-    PQ_LAUNCH_CHECK("encode_gemm_kernel");                                                    \
-    if (B > 0) {                                                                              \
-      encode_fix_kernel<(B > 0 ? B : 1)><<<num_sms() * 4, 256, 0, st>>>(                       \
-          fix_list, fix_count, fix_cap, Ahi, Alo, s.ldk, inv, R, d, bounds, pk, ldb);          \
-      PQ_LAUNCH_CHECK("encode_fix_kernel");                                                   \
-    }                                                                                         \
+    kern<<<grid, kEncThreads, sm, st>>>(mAhi[b], mAlo[b], mBhi, mBlo, (int)m, d, s.BN, s.ntn,  \
+                                        s.nk, s.stages, s.tmem_cols, inv[b], bounds, pk, ldb, \
+                                        rb, yk, Ahi[b], Alo[b], s.ldk, R,                      \
+                                        deferred ? fix_cnt[b] : nullptr, fix_cols[b]);         \
   } break;
       PQ_ENC_CASE(0)
       PQ_ENC_CASE(1)
@@ -718,6 +982,17 @@ static int run_encode(const float* X, int64_t n, int d, const void* planes, cons
       default:
         return fail(PQ_ERR_INVALID, "bits must be one of 1,2,3,4,8 (got %d)", bits);
     }
+    PQ_LAUNCH_CHECK("encode_gemm_kernel");
+    if (side) {
+      PQ_CUDA_TRY(cudaEventRecord(side->gemm[b], st));
+      PQ_CUDA_TRY(cudaStreamWaitEvent(s2, side->gemm[b], 0));
+    }
+    if ((rc = fix(i))) return rc;
+    if (i + 2 < nch && (rc = prep(i + 2))) return rc;
+  }
+  if (side) {
+    PQ_CUDA_TRY(cudaEventRecord(side->end, s2));
+    PQ_CUDA_TRY(cudaStreamWaitEvent(st, side->end, 0));
   }
   return PQ_OK;
 }
@@ -750,8 +1025,9 @@ size_t pq_encode_workspace_bytes(int64_t n, int d) {
   if (d <= 0) return 256;
   const EncShape s = enc_shape(d);
   const size_t ch = (size_t)enc_chunk_rows(n);
-  return align_up(ch * s.ldk * 2, 256) * 2 + align_up(ch * 4, 256) + 256 +
-         (size_t)enc_fix_cap((int64_t)ch, d) * 8 + 1024;
+  const size_t one = align_up(ch * s.ldk * 2, 256) * 2 + align_up(ch * 4, 256) * 2 +
+                     align_up(ch * kFixPerRow * 2, 256);
+  return one * enc_buffers(n) + 1024;
 }
 
 int pq_encode(const float* X, int64_t n, int d, const float* R, const void* planes,

@@ -281,16 +281,28 @@ static int try_scan2(const uint8_t* packed, int64_t ldb, const float* norms, int
                      int bits, int precision, const float* qrot, int nq, const float* cent,
                      int K, float* cand_s, long long* cand_id, cudaStream_t st, int* nblk,
                      bool* used);
+static size_t bt_tables_bytes(int64_t n, int d, int nq);
+static int try_scan_bt(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
+                       int bits, int precision, const float* qrot, int nq, const float* cent,
+                       int K, float* cand_s, long long* cand_id, void* tables,
+                       size_t tables_bytes, cudaStream_t st, int* nblk, bool* used);
 
 // Scan every query against all rows, leaving per-block candidates in ws:
 // list b of query q at (q * nblk + b) * K, *nblk_out <= scan_blocks(n, nq).
-// 4- and 8-bit corpora run the TMA-staged scan (scan2.cu) when it fits.
+// 1-, 2-, 4- and 8-bit corpora of 2^18+ rows run the byte-table scan
+// (scan_bt.cu) when `tables` has room for its tables; other 4- and 8-bit
+// corpora the TMA-staged scan (scan2.cu) when it fits; the rest the generic
+// scan below.
 static int run_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
                     int bits, int precision, const float* qrot, int nq, const float* cent, int K,
-                    float* cand_s, long long* cand_id, cudaStream_t st, int* nblk_out) {
+                    float* cand_s, long long* cand_id, void* tables, size_t tables_bytes,
+                    cudaStream_t st, int* nblk_out) {
   bool used = false;
-  int rc = try_scan2(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent, K, cand_s,
-                     cand_id, st, nblk_out, &used);
+  int rc = try_scan_bt(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent, K, cand_s,
+                       cand_id, tables, tables_bytes, st, nblk_out, &used);
+  if (rc || used) return rc;
+  rc = try_scan2(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent, K, cand_s,
+                 cand_id, st, nblk_out, &used);
   if (rc || used) return rc;
   const int64_t per = scan_rows_per_block(n, nq);
   const int nblk = scan_blocks(n, nq);
@@ -333,16 +345,28 @@ static int large_twostage(const uint8_t* packed, int64_t ldb, const float* norms
 
 extern "C" {
 
+}  // extern "C"
+
+// Candidate lists of the streaming scans (the part of the workspace every
+// scan needs).
+static size_t scan_ws_base(int64_t n, int nq, int k) {
+  const size_t c = (size_t)nq * scan_blocks(n, nq) * k;
+  return align_up(align_up(c * sizeof(float), 256) + c * sizeof(long long) + 512, 256);
+}
+
+extern "C" {
+
 size_t pq_adc_scan_workspace_bytes(int64_t n, int d, int nq, int k) {
-  (void)d;
   if (n <= 0 || nq <= 0 || k <= 0) return 256;
   if (k > PQ_TOPK_MAX) {
     size_t p = 2048;
     while ((int64_t)p < n) p <<= 1;
     return p * sizeof(unsigned long long) + 256;
   }
-  const size_t c = (size_t)nq * scan_blocks(n, nq) * k;
-  return align_up(c * sizeof(float), 256) + c * sizeof(long long) + 512;
+  // + the byte-table scan's tables where it may run (a smaller workspace
+  // holding at least the candidate lists is accepted: the call then uses
+  // the other scans).
+  return scan_ws_base(n, nq, k) + bt_tables_bytes(n, d, nq);
 }
 
 int pq_adc_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d, int bits,
@@ -359,7 +383,8 @@ int pq_adc_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
   PQ_CHECK_ARG(n < (1ll << 31), "n=%lld rows exceed one launch; shard the corpus", (long long)n);
   if (nq == 0) return PQ_OK;
   PQ_CHECK_ARG(qrot && cent && out_scores && out_ids, "null pointer argument");
-  const size_t need = pq_adc_scan_workspace_bytes(n, d, nq, k);
+  const size_t need = k > PQ_TOPK_MAX ? pq_adc_scan_workspace_bytes(n, d, nq, k)
+                                      : scan_ws_base(n, nq, k);
   if (ws_bytes < need || !ws)
     return fail(PQ_ERR_WORKSPACE, "pq_adc_scan needs %zu workspace bytes, got %zu", need, ws_bytes);
   cudaStream_t st = (cudaStream_t)stream;
@@ -371,7 +396,9 @@ int pq_adc_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
   const size_t c = (size_t)nq * nblk * k;
   float* cs = cv.take<float>(c);
   long long* ci = cv.take<long long>(c);
-  rc = run_scan(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent, k, cs, ci, st, &nblk);
+  char* tables = (char*)ws + need;
+  rc = run_scan(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent, k, cs, ci, tables,
+                ws_bytes - need, st, &nblk);
   if (rc) return rc;
   return launch_merge(cs, ci, nblk, k, (long long)nblk * k, k, nq, k, row_offset, out_scores,
                       (long long*)out_ids, st);
@@ -495,8 +522,10 @@ int pq_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
     const size_t c = (size_t)nq * nblk * candidates;
     cs = cv.take<float>(c);
     ci = cv.take<long long>(c);
+    const size_t base = scan_ws_base(n, nq, candidates);
     rc = run_scan(packed, ldb, norms, n, d, bits, coarse_precision, qrot, nq, cent_coarse,
-                  candidates, cs, ci, st, &nblk);
+                  candidates, cs, ci, ws_bytes > base ? (char*)ws + base : nullptr,
+                  ws_bytes > base ? ws_bytes - base : 0, st, &nblk);
   }
   if (rc) return rc;
   const size_t sm = rerank_smem(d, bits, candidates, k);

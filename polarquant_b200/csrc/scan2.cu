@@ -376,12 +376,3 @@ static int try_scan2(const uint8_t* packed, int64_t ldb, const float* norms, int
   *used = true;
   return PQ_OK;
 }
-
-
-
-extern "C" int pq_adc_scan_kernel(int64_t n, int d, int bits, int precision, int nq, int k,
-                                  int64_t ldb) {
-  if (k > PQ_TOPK_MAX) return 3;
-  const S2Plan p = s2_plan(n, d, bits, precision, nq, k, ldb);
-  return (p.ok && precision >= 1 && precision <= bits) ? 2 : 1;
-}

@@ -122,3 +122,29 @@ def test_config5_ivf_n_bits12(gpu):
         if not O.topk_equal_up_to_ties(ids[q][keep], sc[q][keep], ri, rs, rtol=RTOL):
             bad.append(q)
     assert not bad, f"{len(bad)} of {nq} queries differ from the oracle: {bad[:8]}"
+
+
+def test_batched_adc_with_threshold_pilot_pass(gpu):
+    """Corpora of 4M+ rows run the int8 kernel in two passes: the first
+    pass's merged lists seed every query's threshold for the second.  The
+    results must not depend on it: all queries against the exact streaming
+    scan, sampled ones against the oracle's search_batch."""
+    import bench
+    from polarquant_b200 import _lib
+    cfg = dict(bench.WORKLOADS["c4"], d=1024)
+    n, nq, k = (4 << 20) + 777, 300, 64
+    pq, cv, Q = _corpus(cfg, n, nq)
+    rows = cv._device()
+    assert _lib.query("pq_adc_batch_kernel", n, rows.d, 4, 4, k, rows.ldb) == 1
+    GI, GS = pq.search_adc_many(cv, Q, k=k)
+    s, i = pq._scan(rows, pq._rotate(Q, rows.device), k, 4, force="scan")
+    SI, SS = i.cpu().numpy(), s.cpu().numpy()
+    bad = [q for q in range(nq) if not O.topk_equal_up_to_ties(GI[q], GS[q], SI[q], SS[q],
+                                                                rtol=RTOL)]
+    assert not bad, f"{len(bad)} of {nq} queries differ from the exact scan: {bad[:8]}"
+    pick = np.arange(0, nq, 25)
+    RI, RS = O.search_batch_chunked(pq.R, pq.centroids, pq._nested, 4, cv.indices, cv.norms,
+                                    Q[pick], k=k)
+    bad = [int(q) for j, q in enumerate(pick)
+           if not O.topk_equal_up_to_ties(GI[q], GS[q], RI[j], RS[j], rtol=RTOL)]
+    assert not bad, f"{len(bad)} sampled queries differ from the oracle: {bad[:8]}"

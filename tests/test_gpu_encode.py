@@ -216,3 +216,31 @@ def test_pq_file_from_device_rows(gpu, tmp_path, bits, d):
     i1, s1 = pq.search_adc(back, q, k=10)
     np.testing.assert_array_equal(i0, i1)
     np.testing.assert_array_equal(s0, s1)
+
+
+@pytest.mark.parametrize("bits,d", [(4, 256), (8, 128), (3, 200)])
+def test_encode_several_chunks(gpu, bits, d):
+    """Calls spanning several 131,072-row chunks run as a pipeline (the
+    normalise/split of chunk i+1 and the near-boundary fix-ups of chunk i-1 on
+    a side stream while chunk i's GEMM runs), with ping-pong plane buffers;
+    results must equal the one-chunk path's parity: norms bit-identical,
+    codes within the boundary rule, and the tensor-core rotation likewise."""
+    from polarquant_b200 import Quantizer
+    from polarquant_b200.encode import rotate_tc
+    n = 3 * 131072 + 1234
+    rng = np.random.default_rng(bits * 7 + d)
+    X = rng.standard_normal((n, d)).astype(np.float32)
+    X *= np.exp(rng.uniform(np.log(0.5), np.log(2.0), (n, 1))).astype(np.float32)
+    pq = Quantizer(d, bits=bits, seed=42)
+    cv = pq.encode(X)
+    ref, norms = O.encode(X, pq.R, pq.boundaries)
+    np.testing.assert_array_equal(cv.norms, norms)
+    check_codes(cv.indices, ref, X, pq.R, pq.boundaries, bits)
+    # Twice more in a row: buffers and events are reused across calls.
+    for _ in range(2):
+        cv2 = pq.encode(X)
+        np.testing.assert_array_equal(cv2.indices, cv.indices)
+    Y = rotate_tc(pq, X).cpu().numpy()
+    rows = np.r_[0:5, 131070:131075, n - 5:n]
+    exact = X[rows].astype(np.float64) @ pq.R.astype(np.float64).T
+    np.testing.assert_allclose(Y[rows], exact, rtol=1e-6, atol=1e-6 * np.abs(exact).max())
