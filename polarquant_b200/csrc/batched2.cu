@@ -8,7 +8,7 @@
 // only its 128 rows), which bounded the one-CTA kernel.
 //
 // Roles per CTA (448 threads): warp 0 loads this CTA's query planes by TMA
-// (no multicast); in the even CTA warp 1 issues the pair MMAs and in the odd
+// (each CTA its own copy); in the even CTA warp 1 issues the pair MMAs and in the odd
 // CTA it relays "query tile landed" to the even CTA; warps 2-5 run the top-k
 // epilogue of this CTA's 128 queries; warps 6.. decode this CTA's half of the
 // corpus tile.  The even CTA's MMA issuer waits on its own barriers, which the

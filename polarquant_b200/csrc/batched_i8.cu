@@ -35,7 +35,7 @@
 // pairs indexed by the shifted code.
 //
 // Roles per CTA (480 threads): warp 0 loads this CTA's query planes by TMA
-// (no multicast); warp 1 issues the pair MMAs (even CTA) or relays "stage
+// (each CTA its own copy); warp 1 issues the pair MMAs (even CTA) or relays "stage
 // landed" to the even CTA (odd CTA); warps 2-9 run the top-k epilogue of this
 // CTA's 128 queries (two warps per TMEM lane quadrant, one per half of the
 // tile's columns); warps 10-13 decode this CTA's 128 rows of each stage;

@@ -625,12 +625,11 @@ encode_gemm_kernel(const __grid_constant__ CUtensorMap tmAhi, const __grid_const
 }
 
 // Recomputes the coordinates the GEMM epilogue listed (within kFixBand of a
-// boundary) exactly as its inline path does -- f64 dot product of the 22-bit
-// x planes with the f32 R, scaled -- and writes their codes into the packed
+// boundary) as its inline path does -- an f64 dot product of the 22-bit x
+// planes with the f32 R, scaled -- and writes their codes into the packed
 // rows.  One warp per row with listed columns: the row's x (hi + lo, exact
-// in f32, read with 16-byte loads and kept in L1 across the row's entries) is
-// dotted with each listed column of R.  One 128-thread block per SM fits
-// beside the encode GEMM.  A row's codes may share a 32-bit word, so
+// in f32, kept in L1 across the row's entries) is dotted with each listed
+// column of R, with coalesced loads.  A row's codes may share a 32-bit word, so
 // each code is written with an atomic AND (clear its bits) and OR (set
 // them): codes occupy disjoint bits, so the order of the updates does not
 // matter.
@@ -650,52 +649,87 @@ encode_fix_kernel(const int* __restrict__ fix_cnt, const uint16_t* __restrict__ 
        row += warps) {
     const int cnt = min(__ldg(fix_cnt + row), kFixPerRow);
     if (cnt == 0) continue;  // warp-uniform
-    // 16-byte loads: 8 consecutive elements per lane and step (the row's
-    // planes stay in L1 across its listed columns).
-    const uint4* ah = reinterpret_cast<const uint4*>(Ahi + row * ldk);
-    const uint4* al = reinterpret_cast<const uint4*>(Alo + row * ldk);
+    // The row's planes stay in L1 across its listed columns.
+    const uint2* ah = reinterpret_cast<const uint2*>(Ahi + row * ldk);
+    const uint2* al = reinterpret_cast<const uint2*>(Alo + row * ldk);
     const float sinv = __ldg(inv_scale + row);
     uint32_t* rowp = reinterpret_cast<uint32_t*>(packed + row * ldb);
+    // d <= 1024 (d % 4 == 0): the row's x is converted to f64 once and kept in
+    // registers (elements 4m .. 4m+3 of lane l, m = l + 32 t); each listed
+    // column then costs one pass over its R row with all loads in flight.
+    const bool regx = (d & 3) == 0 && d <= 1024;
+    double xd[32];
+    if (regx) {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const int m = lane + 32 * t;
+        uint2 hv = make_uint2(0u, 0u), lv = make_uint2(0u, 0u);
+        if (4 * m < d) {
+          hv = __ldg(ah + m);
+          lv = __ldg(al + m);
+        }
+        const __half* hh = reinterpret_cast<const __half*>(&hv);
+        const __half* ll = reinterpret_cast<const __half*>(&lv);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          xd[4 * t + u] = (double)(__half2float(hh[u]) + __half2float(ll[u]));
+      }
+    }
     for (int k = 0; k < cnt; ++k) {
       const int col = fix_cols[(size_t)row * kFixPerRow + k];
       const float* rr = R + (int64_t)col * d;
-      // Two steps' loads (512 columns of the warp) are in flight before the
-      // first FMA of the pair.
       double acc = 0.0;
-      for (int c0 = 0; 8 * c0 < d; c0 += 64) {
-        uint4 hv[2], lv[2];
-        float4 ra[2], rb[2];
+      if (regx) {
+        const float4* r4 = reinterpret_cast<const float4*>(rr);
+        float4 rv[8];
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          const int c8 = c0 + lane + 32 * t;
-          if (8 * c8 < d) {
-            hv[t] = __ldg(ah + c8);
-            lv[t] = __ldg(al + c8);
-            if (8 * c8 + 8 <= d) {
-              ra[t] = __ldg(reinterpret_cast<const float4*>(rr) + 2 * c8);
-              rb[t] = __ldg(reinterpret_cast<const float4*>(rr) + 2 * c8 + 1);
+        for (int t = 0; t < 8; ++t) {
+          const int m = lane + 32 * t;
+          rv[t] = 4 * m < d ? __ldg(r4 + m) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          acc = fma(xd[4 * t + 0], (double)rv[t].x, acc);
+          acc = fma(xd[4 * t + 1], (double)rv[t].y, acc);
+          acc = fma(xd[4 * t + 2], (double)rv[t].z, acc);
+          acc = fma(xd[4 * t + 3], (double)rv[t].w, acc);
+        }
+      } else if ((d & 3) == 0) {
+        // Lane l takes elements 4m .. 4m+3, m = l + 32 t: the warp's R loads
+        // (16 B a lane) and plane loads (8 B a lane) are contiguous; two
+        // steps' loads are in flight before the first FMA of the pair.
+        const float4* r4 = reinterpret_cast<const float4*>(rr);
+        for (int m0 = 0; 4 * m0 < d; m0 += 64) {
+          float4 rv[2];
+          uint2 hv[2], lv[2];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int m = m0 + lane + 32 * t;
+            if (4 * m < d) {
+              rv[t] = __ldg(r4 + m);
+              hv[t] = __ldg(ah + m);
+              lv[t] = __ldg(al + m);
             } else {
-              float tmp[8];
-#pragma unroll
-              for (int u = 0; u < 8; ++u) tmp[u] = 8 * c8 + u < d ? __ldg(rr + 8 * c8 + u) : 0.f;
-              ra[t] = make_float4(tmp[0], tmp[1], tmp[2], tmp[3]);
-              rb[t] = make_float4(tmp[4], tmp[5], tmp[6], tmp[7]);
+              rv[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+              hv[t] = lv[t] = make_uint2(0u, 0u);
             }
-          } else {
-            hv[t] = lv[t] = make_uint4(0, 0, 0, 0);
-            ra[t] = rb[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const __half* hh = reinterpret_cast<const __half*>(&hv[t]);
+            const __half* ll = reinterpret_cast<const __half*>(&lv[t]);
+            const float r4v[4] = {rv[t].x, rv[t].y, rv[t].z, rv[t].w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              acc = fma((double)(__half2float(hh[u]) + __half2float(ll[u])), (double)r4v[u], acc);
           }
         }
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          const __half* hh = reinterpret_cast<const __half*>(&hv[t]);
-          const __half* ll = reinterpret_cast<const __half*>(&lv[t]);
-          const float r8[8] = {ra[t].x, ra[t].y, ra[t].z, ra[t].w,
-                               rb[t].x, rb[t].y, rb[t].z, rb[t].w};
-#pragma unroll
-          for (int u = 0; u < 8; ++u)
-            acc = fma((double)(__half2float(hh[u]) + __half2float(ll[u])), (double)r8[u], acc);
-        }
+      } else {
+        const __half* hs = Ahi + row * ldk;
+        const __half* ls = Alo + row * ldk;
+        for (int j = lane; j < d; j += 32)
+          acc = fma((double)(__half2float(hs[j]) + __half2float(ls[j])), (double)__ldg(rr + j),
+                    acc);
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -779,9 +813,12 @@ using namespace pqb;
 // Per device: the side stream and events of the encode pipeline (created on
 // first use; the pipeline's enqueue runs under a mutex, so concurrent encode
 // calls from several host threads do not interleave their event records).
+// Streams of the chunk pipeline: the GEMMs on s1 (the device's highest
+// priority, so that as an SM frees up the block scheduler places the next
+// GEMM's CTA before more side-kernel blocks), prep and fix-up on s2.
 struct EncSide {
-  cudaStream_t s2;
-  cudaEvent_t start, prep[2], gemm[2], end;
+  cudaStream_t s1, s2;
+  cudaEvent_t start, prep[2], gemm[2], end1, end2;
   bool ok;
 };
 static EncSide g_enc_side[64];
@@ -793,9 +830,13 @@ static int enc_side(EncSide** out) {
   if (dev < 0 || dev >= 64) return fail(PQ_ERR_CUDA, "device ordinal %d out of range", dev);
   EncSide& e = g_enc_side[dev];
   if (!e.ok) {
-    PQ_CUDA_TRY(cudaStreamCreateWithFlags(&e.s2, cudaStreamNonBlocking));
+    int least = 0, greatest = 0;
+    PQ_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+    PQ_CUDA_TRY(cudaStreamCreateWithPriority(&e.s1, cudaStreamNonBlocking, greatest));
+    PQ_CUDA_TRY(cudaStreamCreateWithPriority(&e.s2, cudaStreamNonBlocking, least));
     PQ_CUDA_TRY(cudaEventCreateWithFlags(&e.start, cudaEventDisableTiming));
-    PQ_CUDA_TRY(cudaEventCreateWithFlags(&e.end, cudaEventDisableTiming));
+    PQ_CUDA_TRY(cudaEventCreateWithFlags(&e.end1, cudaEventDisableTiming));
+    PQ_CUDA_TRY(cudaEventCreateWithFlags(&e.end2, cudaEventDisableTiming));
     for (int i = 0; i < 2; ++i) {
       PQ_CUDA_TRY(cudaEventCreateWithFlags(&e.prep[i], cudaEventDisableTiming));
       PQ_CUDA_TRY(cudaEventCreateWithFlags(&e.gemm[i], cudaEventDisableTiming));
@@ -816,15 +857,12 @@ static void enc_side_carveout(const void* kern) {
                        (int)cudaSharedmemCarveoutMaxShared);
 }
 
-// side: the prep runs beside an encode GEMM, so one 128-thread block per SM
-// (more blocks could take the shared memory the GEMM's next CTA needs).
 static int launch_prep(const float* X, int64_t m, int d, int ldk, __half* Ahi, __half* Alo,
-                       float* inv, float* norms, bool normalize, bool side, cudaStream_t st) {
+                       float* inv, float* norms, bool normalize, cudaStream_t st) {
   const int T = (ldk + 127) / 128;
   if (d % 4 == 0 && ((uintptr_t)X & 15) == 0 && T <= 16) {
     int g = (int)((m + 3) / 4);
-    const int gmax = side ? num_sms() : num_sms() * 32;
-    if (g > gmax) g = gmax;
+    if (g > num_sms() * 32) g = num_sms() * 32;
     switch (T) {
 #define PQ_PREP4(TT)                                                                         \
   case TT:                                                                                   \
@@ -906,12 +944,14 @@ static int run_encode(const float* X, int64_t n, int d, const void* planes, cons
 
   std::unique_lock<std::mutex> lock(g_enc_mu, std::defer_lock);
   EncSide* side = nullptr;
-  cudaStream_t s2 = st;  // one chunk: everything on the caller's stream
+  cudaStream_t s1 = st, s2 = st;  // one chunk: everything on the caller's stream
   if (nbuf == 2) {
     lock.lock();
     if ((rc = enc_side(&side))) return rc;
+    s1 = side->s1;
     s2 = side->s2;
     PQ_CUDA_TRY(cudaEventRecord(side->start, st));
+    PQ_CUDA_TRY(cudaStreamWaitEvent(s1, side->start, 0));
     PQ_CUDA_TRY(cudaStreamWaitEvent(s2, side->start, 0));
   }
   auto chunk_rows = [&](int i) { return (n - (int64_t)i * ch < ch) ? n - (int64_t)i * ch : ch; };
@@ -919,7 +959,7 @@ static int run_encode(const float* X, int64_t n, int d, const void* planes, cons
     const int b = i % nbuf;
     const int64_t r0 = (int64_t)i * ch;
     int r = launch_prep(X + r0 * d, chunk_rows(i), d, s.ldk, Ahi[b], Alo[b], inv[b],
-                        (bits > 0 && norms) ? norms + r0 : nullptr, bits > 0, i > 0, s2);
+                        (bits > 0 && norms) ? norms + r0 : nullptr, bits > 0, s2);
     if (r) return r;
     if (side) PQ_CUDA_TRY(cudaEventRecord(side->prep[b], s2));
     return PQ_OK;
@@ -930,12 +970,10 @@ static int run_encode(const float* X, int64_t n, int d, const void* planes, cons
     const int64_t r0 = (int64_t)i * ch;
     const int64_t m = chunk_rows(i);
     uint8_t* pk = packed + r0 * ldb;
-    // One block per SM when it runs beside the next chunk's GEMM.
-    const int g = nbuf == 2 ? num_sms() : num_sms() * 16;
+    const int g = num_sms() * 4;  // the resident blocks (128 registers a thread)
     switch (bits) {
 #define PQ_FIX_CASE(B)                                                                      \
   case B:                                                                                   \
-    enc_side_carveout((const void*)encode_fix_kernel<B>);                                   \
     encode_fix_kernel<B><<<g, 128, 0, s2>>>(fix_cnt[b], fix_cols[b], m, Ahi[b], Alo[b],     \
                                             s.ldk, inv[b], R, d, bounds, pk, ldb);          \
     break;
@@ -956,18 +994,18 @@ static int run_encode(const float* X, int64_t n, int d, const void* planes, cons
     const int b = i % nbuf;
     const int64_t r0 = (int64_t)i * ch;
     const int64_t m = chunk_rows(i);
-    if (side) PQ_CUDA_TRY(cudaStreamWaitEvent(st, side->prep[b], 0));
+    if (side) PQ_CUDA_TRY(cudaStreamWaitEvent(s1, side->prep[b], 0));
     const int ntiles = (int)((m + kEncBM - 1) / kEncBM) * s.ntn;
     const int grid = ntiles < num_sms() ? ntiles : num_sms();
     uint8_t* pk = packed ? packed + r0 * ldb : nullptr;
     float* yk = Y ? Y + r0 * d : nullptr;
-    if (deferred) PQ_CUDA_TRY(cudaMemsetAsync(fix_cnt[b], 0, sizeof(int) * (size_t)m, st));
+    if (deferred) PQ_CUDA_TRY(cudaMemsetAsync(fix_cnt[b], 0, sizeof(int) * (size_t)m, s1));
     switch (bits) {
 #define PQ_ENC_CASE(B)                                                                        \
   case B: {                                                                                   \
     auto kern = encode_gemm_kernel<B>;                                                        \
     PQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); \
-    kern<<<grid, kEncThreads, sm, st>>>(mAhi[b], mAlo[b], mBhi, mBlo, (int)m, d, s.BN, s.ntn,  \
+    kern<<<grid, kEncThreads, sm, s1>>>(mAhi[b], mAlo[b], mBhi, mBlo, (int)m, d, s.BN, s.ntn,  \
                                         s.nk, s.stages, s.tmem_cols, inv[b], bounds, pk, ldb, \
                                         rb, yk, Ahi[b], Alo[b], s.ldk, R,                      \
                                         deferred ? fix_cnt[b] : nullptr, fix_cols[b]);         \
@@ -984,15 +1022,17 @@ static int run_encode(const float* X, int64_t n, int d, const void* planes, cons
     }
     PQ_LAUNCH_CHECK("encode_gemm_kernel");
     if (side) {
-      PQ_CUDA_TRY(cudaEventRecord(side->gemm[b], st));
+      PQ_CUDA_TRY(cudaEventRecord(side->gemm[b], s1));
       PQ_CUDA_TRY(cudaStreamWaitEvent(s2, side->gemm[b], 0));
     }
     if ((rc = fix(i))) return rc;
     if (i + 2 < nch && (rc = prep(i + 2))) return rc;
   }
   if (side) {
-    PQ_CUDA_TRY(cudaEventRecord(side->end, s2));
-    PQ_CUDA_TRY(cudaStreamWaitEvent(st, side->end, 0));
+    PQ_CUDA_TRY(cudaEventRecord(side->end1, s1));
+    PQ_CUDA_TRY(cudaEventRecord(side->end2, s2));
+    PQ_CUDA_TRY(cudaStreamWaitEvent(st, side->end1, 0));
+    PQ_CUDA_TRY(cudaStreamWaitEvent(st, side->end2, 0));
   }
   return PQ_OK;
 }

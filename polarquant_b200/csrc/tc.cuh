@@ -1,5 +1,5 @@
 // Thin wrappers over the sm_100a PTX used by the tensor-core kernels:
-// mbarriers (with bounded waits), TMA tile loads (no multicast), tcgen05
+// mbarriers (with bounded waits), TMA tile loads (CTA-local), tcgen05
 // TMEM allocation, MMA, commit and TMEM loads, and the shared-memory matrix
 // descriptor for K-major 128-byte-swizzled fp16 tiles.
 #pragma once
@@ -87,7 +87,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 }
 
 // 2-D tiled TMA load of box {x: inner, y: rows} into shared memory,
-// completing on `bar` (complete_tx).  No multicast.
+// completing on `bar` (complete_tx).  Plain, CTA-local form.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
                                             uint32_t bar) {
   asm volatile(

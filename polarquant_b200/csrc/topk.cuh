@@ -1,6 +1,7 @@
 // Block-wide exact top-K with a shared-memory candidate buffer.
 //
-// Threads offer (score, id) pairs in rounds of at most blockDim offers.  A pair
+// Threads offer (score, id) pairs in rounds of at most one offer per thread
+// of the group.  A pair
 // is kept only if it beats the current K-th best of the buffer (the total order
 // of pqb::better); when the buffer could overflow in the next round it is
 // bitonic-sorted and cut back to K.  Rejections are exact: a pair worse than
@@ -11,7 +12,28 @@
 
 namespace pqb {
 
-struct BlockTopK {
+// The threads that share one top-K buffer: the whole CTA ...
+struct CtaGroup {
+  __device__ __forceinline__ int rank() const { return threadIdx.x; }
+  __device__ __forceinline__ int size() const { return blockDim.x; }
+  __device__ __forceinline__ void sync() const { __syncthreads(); }
+};
+
+// ... or NT consecutive threads from `first` (whole warps) meeting at named
+// barrier ID (1..15), while the CTA's other warps do other work.
+template <int ID, int NT>
+struct WarpsGroup {
+  int first;
+  __device__ __forceinline__ int rank() const { return (int)threadIdx.x - first; }
+  __device__ __forceinline__ int size() const { return NT; }
+  __device__ __forceinline__ void sync() const {
+    asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(NT) : "memory");
+  }
+};
+
+template <class G>
+struct TopKT {
+  G g;
   float* s;         // [cap]
   long long* id;    // [cap]
   int* count;       // number of filled slots
@@ -40,12 +62,12 @@ struct BlockTopK {
     count = reinterpret_cast<int*>(tail);
     ts = reinterpret_cast<float*>(tail + 8);
     tid = reinterpret_cast<long long*>(tail + 16);
-    if (threadIdx.x == 0) {
+    if (g.rank() == 0) {
       *count = 0;
       *ts = -INFINITY;
       *tid = -1;
     }
-    __syncthreads();
+    g.sync();
   }
 
   // Called by every thread; `valid` marks whether this thread has an offer.
@@ -60,14 +82,14 @@ struct BlockTopK {
   // Block-wide: bitonic sort of the whole buffer, best first.
   __device__ void sort_all() {
     const int n = *count;
-    for (int i = n + threadIdx.x; i < cap; i += blockDim.x) {
+    for (int i = n + g.rank(); i < cap; i += g.size()) {
       s[i] = -INFINITY;
       id[i] = -1;
     }
-    __syncthreads();
+    g.sync();
     for (int k = 2; k <= cap; k <<= 1) {
       for (int j = k >> 1; j > 0; j >>= 1) {
-        for (int i = threadIdx.x; i < cap; i += blockDim.x) {
+        for (int i = g.rank(); i < cap; i += g.size()) {
           const int l = i ^ j;
           if (l > i) {
             const bool desc = (i & k) == 0;
@@ -80,7 +102,7 @@ struct BlockTopK {
             }
           }
         }
-        __syncthreads();
+        g.sync();
       }
     }
   }
@@ -88,7 +110,7 @@ struct BlockTopK {
   // Block-wide: keep the best K.
   __device__ void compact() {
     sort_all();
-    if (threadIdx.x == 0) {
+    if (g.rank() == 0) {
       int n = *count;
       if (n >= K) {
         n = K;
@@ -97,20 +119,20 @@ struct BlockTopK {
       }
       *count = n;
     }
-    __syncthreads();
+    g.sync();
   }
 
   // Block-wide, after a round of offers: compact if the next round could overflow.
   __device__ __forceinline__ void end_round() {
-    __syncthreads();
-    if (*count > cap - (int)blockDim.x) compact();
+    g.sync();
+    if (*count > cap - (int)g.size()) compact();
   }
 
   // Block-wide: final sort; writes K results (id -1 / -inf past the filled count).
   __device__ void write(float* out_s, long long* out_id, long long id_offset) {
     compact();
     const int n = *count;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+    for (int i = g.rank(); i < K; i += g.size()) {
       if (i < n) {
         out_s[i] = s[i];
         out_id[i] = id[i] + id_offset;
@@ -121,5 +143,7 @@ struct BlockTopK {
     }
   }
 };
+
+using BlockTopK = TopKT<CtaGroup>;
 
 }  // namespace pqb
