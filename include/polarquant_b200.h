@@ -139,8 +139,10 @@ int pq_decode(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n,
 size_t pq_adc_scan_workspace_bytes(int64_t n, int d, int nq, int k);
 /* Which kernel pq_adc_scan runs for this shape (with the workspace that
  * pq_adc_scan_workspace_bytes gives): 4 = byte-table scan (1-, 2-, 4- and
- * 8-bit codes, n >= 2^18, nq <= 64, k <= 512, ldb >= 128: one lookup per
- * packed byte), 2 = TMA-staged streaming scan (4- and 8-bit codes, n >= 256,
+ * 8-bit codes, rows of at most 1024 bytes, n >= 2^18, nq <= 64, k <= 512:
+ * one lookup per packed byte; its workspace holds the byte tables, 1 KB per
+ * byte position per query, and the per-slice row sums of up to 256 MB of
+ * rows), 2 = TMA-staged streaming scan (4- and 8-bit codes, n >= 256,
  * ldb >= 128, table fits in shared memory), 1 = generic streaming scan,
  * 3 = full sort (k > PQ_TOPK_MAX).  Diagnostic.  A workspace smaller than
  * pq_adc_scan_workspace_bytes but holding the candidate lists is accepted:

@@ -497,7 +497,7 @@ int pq_ivf_search(const uint8_t* packed, int64_t ldb, const float* norms, int64_
   PQ_LAUNCH_CHECK("ivf_group_scan_kernel");
   const int parts = splits;
   if (!rerank)  // search_coarse: merged coarse top-k
-    return launch_merge(cs, ci, parts, candidates, (long long)parts * candidates, candidates, nq,
+    return launch_merge_sorted(cs, ci, parts, candidates, (long long)parts * candidates, candidates, nq,
                         k, 0, out_scores, (long long*)out_ids, st);
   const size_t smr = rerank_smem(d, bits, candidates, k);
   PQ_DISPATCH_B(bits, {
@@ -506,7 +506,7 @@ int pq_ivf_search(const uint8_t* packed, int64_t ldb, const float* norms, int64_
     if (rc) return rc;
     kern<<<nq, kScanThreads, smr, st>>>(packed, ldb, norms, n, d, qrot, cent_full, cs, ci, parts,
                                         nullptr, candidates, k, 0, out_scores,
-                                        (long long*)out_ids);
+                                        (long long*)out_ids, 1);
   });
   PQ_LAUNCH_CHECK("rerank_kernel");
   return PQ_OK;

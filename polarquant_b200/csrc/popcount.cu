@@ -149,7 +149,7 @@ int pq_hamming_scan(const uint8_t* signs, int64_t ldb, int64_t n, int d, const f
   int nblk = 0;
   rc = run_hamming(signs, ldb, n, d, qrot, nq, k, cs, ci, &nblk, st);
   if (rc) return rc;
-  return launch_merge(cs, ci, nblk, k, (long long)nblk * k, k, nq, k, row_offset, out_scores,
+  return launch_merge_sorted(cs, ci, nblk, k, (long long)nblk * k, k, nq, k, row_offset, out_scores,
                       (long long*)out_ids, st);
 }
 
@@ -188,7 +188,7 @@ int pq_hamming_twostage(const uint8_t* signs, int64_t ldb_signs, const uint8_t* 
     if (rc) return rc;
     kern<<<nq, kScanThreads, sm, st>>>(packed, ldb, norms, n, d, qrot, cent_full, cs, ci, nblk,
                                        nullptr, candidates, k, row_offset, out_scores,
-                                       (long long*)out_ids);
+                                       (long long*)out_ids, 1);
   });
   PQ_LAUNCH_CHECK("rerank_kernel");
   return PQ_OK;

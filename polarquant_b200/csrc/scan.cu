@@ -81,6 +81,41 @@ merge_topk_kernel(const float* __restrict__ in_s, const long long* __restrict__ 
   tk.write(out_s + (size_t)q * K, out_id + (size_t)q * K, id_offset);
 }
 
+// Merge of lists that are each sorted best first (BlockTopK::write output,
+// padded with id -1): thread t walks list t of a chunk of blockDim lists,
+// offering its elements in order and stopping at the first one the block's
+// top-K rejects (every later element of the list is worse), so a query costs
+// about K + parts offers instead of parts * kin.  Same result as
+// merge_topk_kernel.
+__global__ void __launch_bounds__(kScanThreads)
+merge_sorted_kernel(const float* __restrict__ in_s, const long long* __restrict__ in_id,
+                    int parts, int kin, long long q_stride, long long part_stride, int K,
+                    long long id_offset, float* __restrict__ out_s, long long* __restrict__ out_id) {
+  extern __shared__ __align__(16) char smem[];
+  const int q = blockIdx.x;
+  BlockTopK tk;
+  tk.init(smem, K, BlockTopK::cap_for(K, blockDim.x));
+  for (int p0 = 0; p0 < parts; p0 += blockDim.x) {
+    const int part = p0 + threadIdx.x;
+    bool active = part < parts;
+    const long long row = q * q_stride + (long long)part * part_stride;
+    for (int j = 0; j < kin; ++j) {
+      if (!__syncthreads_or(active)) break;  // block-uniform
+      float sc = 0.f;
+      long long ident = -1;
+      if (active) {
+        ident = in_id[row + j];
+        sc = in_s[row + j];
+      }
+      const bool valid = active && ident >= 0;
+      const bool taken = tk.offer(valid, sc, ident);
+      tk.end_round();
+      active = valid && taken;
+    }
+  }
+  tk.write(out_s + (size_t)q * K, out_id + (size_t)q * K, id_offset);
+}
+
 // Rescoring of a candidate row list at precision P (exact f32 table sums,
 // P = B: full precision), then top-K.  When `coarse` is non-null the list is
 // first selected as the top-C of the per-part candidate lists (two-stage
@@ -91,7 +126,8 @@ rerank_kernel(const uint8_t* __restrict__ packed, int64_t ldb, const float* __re
               int64_t n, int d, const float* __restrict__ qrot, const float* __restrict__ cent_full,
               const float* __restrict__ coarse_s, const long long* __restrict__ coarse_id,
               int coarse_parts, const long long* __restrict__ cand, int C, int K,
-              long long id_offset, float* __restrict__ out_s, long long* __restrict__ out_id) {
+              long long id_offset, float* __restrict__ out_s, long long* __restrict__ out_id,
+              int coarse_sorted) {
   extern __shared__ __align__(16) char smem[];
   const int q = blockIdx.x;
   const size_t st_floats = query_state_floats<P>(d);
@@ -105,7 +141,29 @@ rerank_kernel(const uint8_t* __restrict__ packed, int64_t ldb, const float* __re
     tk.init(tk_mem, C, BlockTopK::cap_for(C, blockDim.x));
     const long long total = (long long)coarse_parts * C;
     const long long qoff = (long long)q * total;
-    for (long long base = 0; base < total; base += blockDim.x) {
+    if (coarse_sorted) {
+      // Lists sorted best first: as merge_sorted_kernel, each thread walks
+      // one list until the top-C rejects an element.
+      for (int p0 = 0; p0 < coarse_parts; p0 += blockDim.x) {
+        const int part = p0 + threadIdx.x;
+        bool active = part < coarse_parts;
+        const long long lrow = qoff + (long long)part * C;
+        for (int j = 0; j < C; ++j) {
+          if (!__syncthreads_or(active)) break;  // block-uniform
+          float sc = 0.f;
+          long long ident = -1;
+          if (active) {
+            ident = coarse_id[lrow + j];
+            sc = coarse_s[lrow + j];
+          }
+          const bool valid = active && ident >= 0;
+          const bool taken = tk.offer(valid, sc, ident);
+          tk.end_round();
+          active = valid && taken;
+        }
+      }
+    }
+    for (long long base = 0; !coarse_sorted && base < total; base += blockDim.x) {
       const long long e = base + threadIdx.x;
       bool valid = e < total;
       float sc = 0.f;
@@ -277,6 +335,20 @@ static int launch_merge(const float* in_s, const long long* in_id, int parts, in
   return PQ_OK;
 }
 
+// launch_merge for lists each sorted best first (the scans' BlockTopK lists).
+static int launch_merge_sorted(const float* in_s, const long long* in_id, int parts, int kin,
+                               long long q_stride, long long part_stride, int nq, int K,
+                               long long id_offset, float* out_s, long long* out_id,
+                               cudaStream_t st) {
+  const size_t sm = BlockTopK::smem_bytes(BlockTopK::cap_for(K, kScanThreads));
+  int rc = set_smem(merge_sorted_kernel, sm);
+  if (rc) return rc;
+  merge_sorted_kernel<<<nq, kScanThreads, sm, st>>>(in_s, in_id, parts, kin, q_stride,
+                                                    part_stride, K, id_offset, out_s, out_id);
+  PQ_LAUNCH_CHECK("merge_sorted_kernel");
+  return PQ_OK;
+}
+
 static int try_scan2(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
                      int bits, int precision, const float* qrot, int nq, const float* cent,
                      int K, float* cand_s, long long* cand_id, cudaStream_t st, int* nblk,
@@ -400,8 +472,8 @@ int pq_adc_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
   rc = run_scan(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent, k, cs, ci, tables,
                 ws_bytes - need, st, &nblk);
   if (rc) return rc;
-  return launch_merge(cs, ci, nblk, k, (long long)nblk * k, k, nq, k, row_offset, out_scores,
-                      (long long*)out_ids, st);
+  return launch_merge_sorted(cs, ci, nblk, k, (long long)nblk * k, k, nq, k, row_offset,
+                             out_scores, (long long*)out_ids, st);
 }
 
 // Query batches at least this large run the coarse stage of two-stage search
@@ -460,7 +532,7 @@ static int rescore_candidates(const uint8_t* packed, int64_t ldb, const float* n
     rc = set_smem(kern, sm);
     if (rc) return rc;
     kern<<<nq, kScanThreads, sm, st>>>(packed, ldb, norms, n, d, qrot, cent, cs, ci, parts,
-                                       nullptr, C, K, id_offset, out_s, out_id);
+                                       nullptr, C, K, id_offset, out_s, out_id, 0);
   });
   PQ_LAUNCH_CHECK("rerank_kernel");
   return PQ_OK;
@@ -490,6 +562,9 @@ int pq_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
   float* cs;
   long long* ci;
   int nblk;
+  // The streaming scans' candidate lists are sorted best first (BlockTopK
+  // output); the batched kernels' are not.
+  const int sorted_lists = twostage_batched(n, nq, candidates) ? 0 : 1;
   if (twostage_batched(n, nq, candidates)) {
     int kpart = candidates;
     rc = run_batched(packed, ldb, norms, n, d, bits, coarse_precision, qrot, nq, cent_coarse,
@@ -511,7 +586,7 @@ int pq_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
         if (rc) return rc;
         kern<<<nq, kScanThreads, sm, st>>>(packed, ldb, norms, n, d, qrot, cent_full, nullptr,
                                            nullptr, 0, ei, candidates, k, row_offset, out_scores,
-                                           (long long*)out_ids);
+                                           (long long*)out_ids, 0);
       });
       PQ_LAUNCH_CHECK("rerank_kernel");
       return PQ_OK;
@@ -535,7 +610,7 @@ int pq_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
     if (rc) return rc;
     kern<<<nq, kScanThreads, sm, st>>>(packed, ldb, norms, n, d, qrot, cent_full, cs, ci, nblk,
                                        nullptr, candidates, k, row_offset, out_scores,
-                                       (long long*)out_ids);
+                                       (long long*)out_ids, sorted_lists);
   });
   PQ_LAUNCH_CHECK("rerank_kernel");
   return PQ_OK;
@@ -560,7 +635,7 @@ int pq_rerank(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n,
     if (rc) return rc;
     kern<<<nq, kScanThreads, sm, st>>>(packed, ldb, norms, n, d, qrot, cent_full, nullptr, nullptr,
                                        0, (const long long*)cand, C, k, row_offset, out_scores,
-                                       (long long*)out_ids);
+                                       (long long*)out_ids, 0);
   });
   PQ_LAUNCH_CHECK("rerank_kernel");
   return PQ_OK;

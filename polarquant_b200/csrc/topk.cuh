@@ -71,12 +71,15 @@ struct TopKT {
   }
 
   // Called by every thread; `valid` marks whether this thread has an offer.
-  __device__ __forceinline__ void offer(bool valid, float sc, long long ident) {
+  // Returns whether the pair went into the buffer.
+  __device__ __forceinline__ bool offer(bool valid, float sc, long long ident) {
     if (valid && (*tid < 0 || better(sc, ident, *ts, *tid))) {
       int slot = atomicAdd(count, 1);
       s[slot] = sc;
       id[slot] = ident;
+      return true;
     }
+    return false;
   }
 
   // Block-wide: bitonic sort of the whole buffer, best first.
