@@ -85,10 +85,10 @@ CHUNK = 65536
 
 # DRAM bytes (read + write) per launch of the dominant batched-ADC kernel,
 # from an ncu capture of pair_i8_kernel on the 4M-row slice of the d=1536
-# workload at 10,000 queries (18.6 GB read + 1.9 GB written), scaled to other
+# workload at 10,000 queries (27.6 GB read + 2.06 GB written), scaled to other
 # row counts of the same workload by rows (traffic grows with the row tiles at
 # a fixed query batch).
-PROFILED_TRAFFIC = {"rows": 4_000_000, "bytes": 20.52e9, "queries": 10_000, "d": 1536,
+PROFILED_TRAFFIC = {"rows": 4_000_000, "bytes": 29.67e9, "queries": 10_000, "d": 1536,
                     "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of "
                               "pair_i8_kernel on the 4M-row slice, scaled by rows"}
 
@@ -457,7 +457,7 @@ def encode_reference_line(args, cfg, torch, dev, world):
 def scan_kernel_name(rows, nq, k, p):
     from polarquant_b200 import _lib
     kind = _lib.query("pq_adc_scan_kernel", rows.n, rows.d, rows.bits, p, nq, k, rows.ldb)
-    return {4: "scan_bt_kernel (byte tables)", 2: "scan2_kernel (TMA-staged)",
+    return {4: "scan_bt_kernel (byte tables) + bt_score_kernel", 2: "scan2_kernel (TMA-staged)",
             1: "scan_topk_kernel", 3: "score_keys + sort"}.get(
         kind, "?")
 
@@ -692,7 +692,7 @@ def search_workload(args, cfg, torch, dist, dev, world, rank, steps, warmup, hea
                            "frac": sgbs / pk["hbm"], "queries_per_launch": nsq,
                            "launch_ms": sms,
                            "kernel": scan_kernel_name(rows, nsq, k_scan, p_scan) +
-                                     " + merge_topk_kernel, one corpus pass per query",
+                                     " + merge, whole pq_adc_scan call, one corpus pass per query",
                            "peak_kind": pk["kind"], "alg_bytes_per_launch": sbytes,
                            "alg_bytes_basis": "row_bytes + 4 per row per query"}
     scan_roof = scan_roofs[1]

@@ -24,7 +24,7 @@
 // partial sums would not fit the buffer are scanned in row chunks.
 //
 // Lookups: lane 8*rho + g of a consumer warp holds the 16-byte group g of row
-// rho (4 rows per warp instruction, four such row groups per warp and stage).
+// rho (4 rows per warp instruction, two such row groups per warp and stage).
 // At step (k, i') it looks up byte i = (i' + rho) mod 4 of word k, byte
 // position p = 16g + 4k + i.  Position p has its 256 entries in bank 4g + i,
 // so the 32 lanes of every lookup hit 32 banks whatever the codes.  The table
@@ -32,7 +32,7 @@
 // lookup address is the lane's base with byte 1 replaced by the code byte:
 // one PRMT per lookup, and one packed f32x2 add per two rows' lookups.
 //
-// Warp roles (288 threads): warps 0-7 consume stages (16 rows each), warp 8
+// Warp roles (544 threads): warps 0-15 consume stages (8 rows each), warp 16
 // issues the TMA loads.  Every wait is bounded; a CTA that gives up records
 // the error, stops issuing and waits for its copies in flight.
 #include "codes.cuh"
@@ -41,9 +41,9 @@
 
 namespace pqb {
 
-constexpr int kBtConsumerWarps = 8;
-constexpr int kBtProducerWarp = 8;
-constexpr int kBtThreads = 32 * (kBtConsumerWarps + 1);  // 288
+constexpr int kBtConsumerWarps = 16;
+constexpr int kBtProducerWarp = 16;
+constexpr int kBtThreads = 32 * (kBtConsumerWarps + 1);  // 544
 constexpr int kBtSlab = 128;                      // bytes of a row slice (one CTA)
 constexpr int kBtRows = 128;                      // rows per stage
 constexpr uint32_t kBtStage = kBtRows * kBtSlab;  // 16 KB
@@ -314,68 +314,46 @@ scan_bt_kernel(const __grid_constant__ CUtensorMap tmap, const float* __restrict
                                   bt_wait(TBAR, 0u, abort_flag, tc::kErrWaitTmaFull));
     int slot = 0;
     uint32_t fph = 0;
-    // This lane's 16 bytes of row 16 warp + rho in ring slot 0 (the slot's
-    // address advances with the slot); lanes 2j (rho = 0) store rows
-    // 16 warp + 4j .. +3 of each stage.
-    const uint32_t lane_off = (uint32_t)(16 * warp + rho) * kBtSlab + 16u * g;
+    // This lane's 16 bytes of row 8 warp + rho in ring slot 0 (the slot's
+    // address advances with the slot); lanes 0 and 4 store rows 8 warp .. +3
+    // and 8 warp + 4 .. +7 of each stage.
+    const uint32_t lane_off = (uint32_t)(8 * warp + rho) * kBtSlab + 16u * g;
     uint32_t ra = slot_addr(0) + lane_off;
-    float* pout = P + ((size_t)q * C + rank) * pstride + row0 + 16 * warp + 4 * (g >> 1);
+    float* pout = P + ((size_t)q * C + rank) * pstride + row0 + 8 * warp + 4 * (g >> 2);
     for (int L = 0; L < T && ok; ++L) {
       if (!__all_sync(0xffffffffu,
                       bt_wait(FULL + 8u * slot, fph, abort_flag, tc::kErrWaitTmaFull)))
         break;
-      // Rows 16 warp + 4 j + rho of the stage, j = 0..3.
-      uint32_t w[4][4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint4 x = bt_lds128(ra + (uint32_t)(4 * j) * kBtSlab);
-        w[j][0] = x.x;
-        w[j][1] = x.y;
-        w[j][2] = x.z;
-        w[j][3] = x.w;
-      }
-      float a[4][4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-#pragma unroll
-        for (int ip = 0; ip < 4; ++ip) a[j][ip] = 0.f;
+      // Rows 8 warp + 4 j + rho of the stage, j = 0, 1.
+      const uint4 x0 = bt_lds128(ra), x1 = bt_lds128(ra + 4u * kBtSlab);
+      const uint32_t w0[4] = {x0.x, x0.y, x0.z, x0.w}, w1[4] = {x1.x, x1.y, x1.z, x1.w};
+      float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
 #pragma unroll
-        for (int ip = 0; ip < 4; ++ip) {
-          bt_add2(a[0][ip], a[1][ip], bt_lds(__byte_perm(w[0][k], base_a[k][ip], sel[ip])),
-                  bt_lds(__byte_perm(w[1][k], base_a[k][ip], sel[ip])));
-          bt_add2(a[2][ip], a[3][ip], bt_lds(__byte_perm(w[2][k], base_a[k][ip], sel[ip])),
-                  bt_lds(__byte_perm(w[3][k], base_a[k][ip], sel[ip])));
-        }
+        for (int ip = 0; ip < 4; ++ip)
+          bt_add2(a0[ip], a1[ip], bt_lds(__byte_perm(w0[k], base_a[k][ip], sel[ip])),
+                  bt_lds(__byte_perm(w1[k], base_a[k][ip], sel[ip])));
       }
       // The slab is consumed (its words are in registers).
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(EMPTY + 8u * slot);
-      float r[4];
-#pragma unroll
-      for (int j = 0; j < 4; j += 2) {
-        bt_add2(a[j][0], a[j + 1][0], a[j][1], a[j + 1][1]);
-        bt_add2(a[j][2], a[j + 1][2], a[j][3], a[j + 1][3]);
-        bt_add2(a[j][0], a[j + 1][0], a[j][2], a[j + 1][2]);
-        r[j] = a[j][0];
-        r[j + 1] = a[j + 1][0];
-      }
-      // Transposed reduction over the 8 lanes of each row: lane g ends with
-      // row j = g >> 1's slice sum (g even).
-      const bool h4 = (g & 4) != 0, h2 = (g & 2) != 0;
-      const float k0 = h4 ? r[2] : r[0], k1 = h4 ? r[3] : r[1];
-      const float s0 = h4 ? r[0] : r[2], s1 = h4 ? r[1] : r[3];
-      const float u0 = k0 + __shfl_xor_sync(0xffffffffu, s0, 4);
-      const float u1 = k1 + __shfl_xor_sync(0xffffffffu, s1, 4);
-      float v = (h2 ? u1 : u0) + __shfl_xor_sync(0xffffffffu, h2 ? u0 : u1, 2);
+      bt_add2(a0[0], a1[0], a0[1], a1[1]);
+      bt_add2(a0[2], a1[2], a0[3], a1[3]);
+      bt_add2(a0[0], a1[0], a0[2], a1[2]);
+      const float r0 = a0[0], r1 = a1[0];
+      // Transposed reduction over the 8 lanes of each row: lanes g < 4 end
+      // with row j = 0's slice sum, g >= 4 with row j = 1's.
+      const bool up = (g & 4) != 0;
+      float v = (up ? r1 : r0) + __shfl_xor_sync(0xffffffffu, up ? r0 : r1, 4);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
       v += __shfl_xor_sync(0xffffffffu, v, 1);
-      // Rows 16 warp + 4 j .. +3 (rho = 0..3) are in lanes 8 rho + 2 j: lane
-      // 2 j gathers them and stores 16 bytes.
+      // Rows 8 warp + 4 j .. +3 (rho = 0..3) are in lanes 8 rho + 4 j: lane
+      // 4 j gathers them and stores 16 bytes.
       const float v1 = __shfl_down_sync(0xffffffffu, v, 8);
       const float v2 = __shfl_down_sync(0xffffffffu, v, 16);
       const float v3 = __shfl_down_sync(0xffffffffu, v, 24);
-      if (lane < 8 && (g & 1) == 0)
+      if (lane < 8 && (g & 3) == 0)
         *reinterpret_cast<float4*>(pout + (int64_t)L * kBtRows) = make_float4(v, v1, v2, v3);
       if (++slot == S) {
         slot = 0;
@@ -403,6 +381,128 @@ scan_bt_kernel(const __grid_constant__ CUtensorMap tmap, const float* __restrict
 // of each row added in slice order, times the row's norm -- and writes its
 // top-K to candidate list list0 + b of query q.
 constexpr int kBtScoreThreads = 512;
+constexpr int kBtSelectWords = 264;  // selection scratch: histogram, bin, counts, tie id
+constexpr int kBtScoreGroup = 4;  // rounds whose loads are in flight together
+
+// Order-preserving map of a score to 32 bits (a larger score gives a larger
+// key; -0 and +0 share a key, as they compare equal; NaN, which `better`
+// never prefers, gets the lowest).
+__device__ __forceinline__ uint32_t bt_fkey(float f) {
+  if (f != f) return 0u;
+  if (f == 0.f) f = 0.f;
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__device__ __forceinline__ float bt_key_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// Block-wide replacement of BlockTopK::compact for a buffer of n > K entries
+// (n <= 2 x blockDim): keeps the best K under `better` without sorting them.
+// A radix selection (4 passes of 8 bits) finds the key T of the K-th best
+// score and how many entries with key T are kept; among those, the ones with
+// the smallest ids (unsigned, as `better`) stay.  The threshold becomes the
+// K-th best entry.  sh: kBtSelectWords words of shared memory.
+__device__ void bt_select_compact(BlockTopK& tk, uint32_t* sh) {
+  constexpr int E = 2;
+  const int n = *tk.count, K = tk.K, t = threadIdx.x, nt = blockDim.x;
+  float es[E];
+  long long ei[E];
+  uint32_t ek[E];
+  bool ev[E];
+#pragma unroll
+  for (int u = 0; u < E; ++u) {
+    const int i = t + u * nt;
+    ev[u] = i < n;
+    es[u] = ev[u] ? tk.s[i] : 0.f;
+    ei[u] = ev[u] ? tk.id[i] : -1;
+    ek[u] = ev[u] ? bt_fkey(es[u]) : 0u;
+  }
+  uint32_t prefix = 0;
+  int remaining = K;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int b = t; b < 256; b += nt) sh[b] = 0u;
+    __syncthreads();
+    const uint32_t hmask = shift == 24 ? 0u : (0xffffffffu << (shift + 8));
+#pragma unroll
+    for (int u = 0; u < E; ++u)
+      if (ev[u] && (ek[u] & hmask) == (prefix & hmask)) atomicAdd(&sh[(ek[u] >> shift) & 255u], 1u);
+    __syncthreads();
+    if (t < 32) {
+      // Lane l holds bins 255 - 8l .. 248 - 8l (descending keys).
+      uint32_t c[8], sum = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = sh[255 - 8 * t - j];
+        sum += c[j];
+      }
+      uint32_t incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (t >= o) incl += y;
+      }
+      const uint32_t excl = incl - sum, rem = (uint32_t)remaining;
+      if (excl < rem && rem <= incl) {
+        uint32_t acc = excl;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (acc < rem && rem <= acc + c[j]) {
+            sh[256] = (uint32_t)(255 - 8 * t - j);
+            sh[257] = rem - acc;
+          }
+          acc += c[j];
+        }
+      }
+    }
+    __syncthreads();
+    prefix |= sh[256] << shift;
+    remaining = (int)sh[257];
+    __syncthreads();
+  }
+  const uint32_t T = prefix;
+  const uint32_t eq = sh[T & 255u];  // entries with key T (the last pass's bin)
+  const int need = remaining;        // of which the first `need` by id stay
+  bool keep[E];
+#pragma unroll
+  for (int u = 0; u < E; ++u) {
+    keep[u] = ev[u] && ek[u] > T;
+    if (ev[u] && ek[u] == T) {
+      if ((int)eq == need) {
+        keep[u] = true;
+      } else {
+        int rank = 0;
+        for (int j = 0; j < n; ++j)
+          if (bt_fkey(tk.s[j]) == T &&
+              (unsigned long long)tk.id[j] < (unsigned long long)ei[u])
+            ++rank;
+        keep[u] = rank < need;
+      }
+    }
+  }
+  unsigned long long* worst = reinterpret_cast<unsigned long long*>(sh + 260);
+  if (t == 0) {
+    sh[258] = 0u;
+    *worst = 0ull;
+  }
+  __syncthreads();  // every entry was read before the buffer is rewritten
+#pragma unroll
+  for (int u = 0; u < E; ++u) {
+    if (!keep[u]) continue;
+    const uint32_t slot = atomicAdd(&sh[258], 1u);
+    tk.s[slot] = es[u];
+    tk.id[slot] = ei[u];
+    if (ek[u] == T) atomicMax(worst, (unsigned long long)ei[u]);
+  }
+  __syncthreads();
+  if (t == 0) {
+    *tk.count = K;
+    *tk.ts = bt_key_float(T);
+    *tk.tid = (long long)*worst;
+  }
+  __syncthreads();
+}
 
 __global__ void __launch_bounds__(kBtScoreThreads)
 bt_score_kernel(const float* __restrict__ P, int64_t pstride, int C,
@@ -411,34 +511,49 @@ bt_score_kernel(const float* __restrict__ P, int64_t pstride, int C,
                 long long* __restrict__ cand_id) {
   extern __shared__ __align__(16) char tk_smem[];
   BlockTopK tk;
-  tk.init(tk_smem, K, BlockTopK::cap_for(K, kBtScoreThreads));
+  const int cap = BlockTopK::cap_for(K, kBtScoreThreads);
+  tk.init(tk_smem, K, cap);
+  uint32_t* sel_scratch = reinterpret_cast<uint32_t*>(tk_smem + BlockTopK::smem_bytes(cap));
   const int q = blockIdx.y;
   const int64_t r0 = (int64_t)blockIdx.x * per2, r1 = min(rows, r0 + per2);
   const float* pq = P + (size_t)q * C * pstride;
-  // Each round's C sums and norm are loaded one round ahead (all in flight
-  // at once), so their latency overlaps the previous round's top-K.
-  float v[kBtMaxSlices], nv = 0.f;
-  auto load = [&](int64_t r, float (&x)[kBtMaxSlices], float& nx) {
-    const bool ok = r < r1;
+  // Rows go in groups of kBtScoreGroup rounds: the next group's slice sums
+  // and norms (up to 9 x kBtScoreGroup loads a thread) are in flight while
+  // the current group's scores are offered to the top-K.
+  constexpr int G = kBtScoreGroup, T = kBtScoreThreads;
+  float xr[G][kBtMaxSlices], nr[G], cur[G];
+  auto issue = [&](int64_t g0) {
 #pragma unroll
-    for (int c = 0; c < kBtMaxSlices; ++c)
-      x[c] = (ok && c < C) ? __ldg(pq + (size_t)c * pstride + r) : 0.f;
-    nx = ok ? __ldg(norms + base + r) : 0.f;
+    for (int u = 0; u < G; ++u) {
+      const int64_t r = g0 + (int64_t)u * T + threadIdx.x;
+      const bool ok = r < r1;
+#pragma unroll
+      for (int c = 0; c < kBtMaxSlices; ++c)
+        xr[u][c] = (ok && c < C) ? __ldg(pq + (size_t)c * pstride + r) : 0.f;
+      nr[u] = ok ? __ldg(norms + base + r) : 0.f;
+    }
   };
-  load(r0 + threadIdx.x, v, nv);
-  for (int64_t b0 = r0; b0 < r1; b0 += kBtScoreThreads) {  // the same trip count in every thread
-    const int64_t r = b0 + threadIdx.x;
-    float w[kBtMaxSlices], nw;
-    load(r + kBtScoreThreads, w, nw);
-    float s = 0.f;
+  auto finish = [&]() {
 #pragma unroll
-    for (int c = 0; c < kBtMaxSlices; ++c) s += v[c];  // slice order (zeros past C)
-    s *= nv;
-    tk.offer(r < r1, s, base + r);
-    tk.end_round();
+    for (int u = 0; u < G; ++u) {
+      float s = 0.f;
 #pragma unroll
-    for (int c = 0; c < kBtMaxSlices; ++c) v[c] = w[c];
-    nv = nw;
+      for (int c = 0; c < kBtMaxSlices; ++c) s += xr[u][c];  // slice order (zeros past C)
+      cur[u] = s * nr[u];
+    }
+  };
+  issue(r0);
+  finish();
+  for (int64_t g0 = r0; g0 < r1; g0 += (int64_t)G * T) {  // the same trip count in every thread
+    issue(g0 + (int64_t)G * T);
+#pragma unroll
+    for (int u = 0; u < G; ++u) {
+      const int64_t r = g0 + (int64_t)u * T + threadIdx.x;
+      tk.offer(r < r1, cur[u], base + r);
+      __syncthreads();
+      if (*tk.count > cap - kBtScoreThreads) bt_select_compact(tk, sel_scratch);
+    }
+    finish();
   }
   const size_t o = ((size_t)q * nlists + list0 + blockIdx.x) * K;
   tk.write(cand_s + o, cand_id + o, 0);
@@ -526,7 +641,7 @@ static BtPlan bt_plan(int64_t n, int d, int bits, int nq, int K, int64_t ldb, si
   // shared by the chunks.
   const int lists = scan_blocks(n, nq) / p.chunks;
   if (lists < 1) return p;
-  int nb2 = (2 * sms + nq - 1) / nq;
+  int nb2 = (sms + nq - 1) / nq;  // one scoring block per SM: fewer top-K compactions
   if (nb2 > lists) nb2 = lists;
   const int64_t minper = 4 * kBtScoreThreads;  // rows per scoring block at least
   const int64_t cap = (p.chunk + minper - 1) / minper;
@@ -585,7 +700,8 @@ static int try_scan_bt(const uint8_t* packed, int64_t ldb, const float* norms, i
   PQ_LAUNCH_CHECK("bt_table_kernel");
   int rc = set_smem(scan_bt_kernel, kBtSmem);
   if (rc) return rc;
-  const size_t tk_smem = BlockTopK::smem_bytes(BlockTopK::cap_for(K, kBtScoreThreads));
+  const size_t tk_smem = BlockTopK::smem_bytes(BlockTopK::cap_for(K, kBtScoreThreads)) +
+                         kBtSelectWords * sizeof(uint32_t);
   rc = set_smem(bt_score_kernel, tk_smem);
   if (rc) return rc;
   const int nlists = p.chunks * p.nb2;

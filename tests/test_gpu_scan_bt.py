@@ -53,3 +53,32 @@ def test_byte_table_scan_matches_oracle(gpu, bits, d, prec, k, nq):
         table = np.outer(pq.R @ Q[q], cent).astype(np.float32)
         sc = O.adc_scores(table, O.resolve_indices(idx[GI[q]], bits, prec), norms[GI[q]])
         np.testing.assert_allclose(GS[q], sc, rtol=RTOL, atol=RTOL * np.abs(sc).max())
+
+
+def test_byte_table_scan_in_row_chunks(gpu):
+    """64 queries over 2^20 + 777 rows of 256 bytes: the per-slice row sums
+    (64 x 2 slices x 4 B per row) exceed the scan's 256 MB buffer, so the
+    rows are streamed and scored in three chunks whose candidate lists share
+    the merge.  Two queries against the oracle's search_adc, all of them
+    through the oracle's ADC scores of the returned rows."""
+    from polarquant_b200 import CompressedVectors, Quantizer, _lib
+    bits, d, nq, k = 4, 512, 64, 50
+    n = (1 << 20) + 777
+    rng = np.random.default_rng(11)
+    idx = rng.integers(0, 1 << bits, size=(n, d), dtype=np.uint8)
+    norms = rng.uniform(0.5, 2.0, n).astype(np.float32)
+    Q = rng.standard_normal((nq, d)).astype(np.float32)
+    pq = Quantizer(d, bits=bits, seed=5)
+    cv = CompressedVectors(idx, norms, d, bits)
+    rows = cv._device()
+    assert _lib.query("pq_adc_scan_kernel", n, d, bits, bits, nq, k, rows.ldb) == 4
+    s, i = pq._scan(rows, pq._rotate(Q, rows.device), k, bits, force="scan")
+    GS, GI = s.cpu().numpy(), i.cpu().numpy()
+    for q in (0, nq - 1):
+        ri, rs = O.search_adc(pq.R, pq.centroids, pq._nested, bits, idx, norms, Q[q], k=k)
+        assert O.topk_equal_up_to_ties(GI[q], GS[q], ri, rs, rtol=RTOL), q
+    for q in range(nq):
+        assert np.all(np.diff(GS[q]) <= 0)
+        table = np.outer(pq.R @ Q[q], pq.centroids).astype(np.float32)
+        sc = O.adc_scores(table, idx[GI[q]], norms[GI[q]])
+        np.testing.assert_allclose(GS[q], sc, rtol=RTOL, atol=RTOL * np.abs(sc).max())
