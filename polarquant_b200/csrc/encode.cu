@@ -645,47 +645,36 @@ encode_fix_kernel(const int* __restrict__ fix_cnt, const uint16_t* __restrict__ 
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  // d <= 1024 (d % 4 == 0): the row's x is converted to f64 once and kept in
-  // registers (elements 4m .. 4m+3 of lane l, m = l + 32 t); each listed
-  // column then costs one pass over its R row with all loads in flight, and
-  // the next row's planes are loaded while this row's columns are computed.
-  const bool regx = (d & 3) == 0 && d <= 1024;
-  uint2 nh[8], nl[8];
-  auto load_planes = [&](int64_t r) {
-    const uint2* ah = reinterpret_cast<const uint2*>(Ahi + r * ldk);
-    const uint2* al = reinterpret_cast<const uint2*>(Alo + r * ldk);
-#pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      const int mm = lane + 32 * t;
-      nh[t] = nl[t] = make_uint2(0u, 0u);
-      if (regx && r < m && 4 * mm < d) {
-        nh[t] = __ldg(ah + mm);
-        nl[t] = __ldg(al + mm);
-      }
-    }
-  };
-  int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
-  load_planes(row);
-  for (; row < m; row += warps) {
+  for (int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); row < m;
+       row += warps) {
     const int cnt = min(__ldg(fix_cnt + row), kFixPerRow);
+    if (cnt == 0) continue;  // warp-uniform
+    // The row's planes stay in L1 across its listed columns.
+    const uint2* ah = reinterpret_cast<const uint2*>(Ahi + row * ldk);
+    const uint2* al = reinterpret_cast<const uint2*>(Alo + row * ldk);
+    const float sinv = __ldg(inv_scale + row);
+    uint32_t* rowp = reinterpret_cast<uint32_t*>(packed + row * ldb);
+    // d <= 1024 (d % 4 == 0): the row's x is converted to f64 once and kept in
+    // registers (elements 4m .. 4m+3 of lane l, m = l + 32 t); each listed
+    // column then costs one pass over its R row with all loads in flight.
+    const bool regx = (d & 3) == 0 && d <= 1024;
     double xd[32];
     if (regx) {
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
-        const __half* hh = reinterpret_cast<const __half*>(&nh[t]);
-        const __half* ll = reinterpret_cast<const __half*>(&nl[t]);
+        const int m = lane + 32 * t;
+        uint2 hv = make_uint2(0u, 0u), lv = make_uint2(0u, 0u);
+        if (4 * m < d) {
+          hv = __ldg(ah + m);
+          lv = __ldg(al + m);
+        }
+        const __half* hh = reinterpret_cast<const __half*>(&hv);
+        const __half* ll = reinterpret_cast<const __half*>(&lv);
 #pragma unroll
         for (int u = 0; u < 4; ++u)
           xd[4 * t + u] = (double)(__half2float(hh[u]) + __half2float(ll[u]));
       }
     }
-    load_planes(row + warps);
-    if (cnt == 0) continue;  // warp-uniform
-    // Without regx the row's planes are read per listed column (from L1).
-    const uint2* ah = reinterpret_cast<const uint2*>(Ahi + row * ldk);
-    const uint2* al = reinterpret_cast<const uint2*>(Alo + row * ldk);
-    const float sinv = __ldg(inv_scale + row);
-    uint32_t* rowp = reinterpret_cast<uint32_t*>(packed + row * ldb);
     for (int k = 0; k < cnt; ++k) {
       const int col = fix_cols[(size_t)row * kFixPerRow + k];
       const float* rr = R + (int64_t)col * d;
@@ -981,7 +970,7 @@ static int run_encode(const float* X, int64_t n, int d, const void* planes, cons
     const int64_t r0 = (int64_t)i * ch;
     const int64_t m = chunk_rows(i);
     uint8_t* pk = packed + r0 * ldb;
-    const int g = num_sms() * 3;  // the resident blocks (168 registers a thread)
+    const int g = num_sms() * 4;  // the resident blocks (128 registers a thread)
     switch (bits) {
 #define PQ_FIX_CASE(B)                                                                      \
   case B:                                                                                   \
