@@ -381,128 +381,7 @@ scan_bt_kernel(const __grid_constant__ CUtensorMap tmap, const float* __restrict
 // of each row added in slice order, times the row's norm -- and writes its
 // top-K to candidate list list0 + b of query q.
 constexpr int kBtScoreThreads = 512;
-constexpr int kBtSelectWords = 264;  // selection scratch: histogram, bin, counts, tie id
 constexpr int kBtScoreGroup = 4;  // rounds whose loads are in flight together
-
-// Order-preserving map of a score to 32 bits (a larger score gives a larger
-// key; -0 and +0 share a key, as they compare equal; NaN, which `better`
-// never prefers, gets the lowest).
-__device__ __forceinline__ uint32_t bt_fkey(float f) {
-  if (f != f) return 0u;
-  if (f == 0.f) f = 0.f;
-  const uint32_t b = __float_as_uint(f);
-  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
-
-__device__ __forceinline__ float bt_key_float(uint32_t k) {
-  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
-}
-
-// Block-wide replacement of BlockTopK::compact for a buffer of n > K entries
-// (n <= 2 x blockDim): keeps the best K under `better` without sorting them.
-// A radix selection (4 passes of 8 bits) finds the key T of the K-th best
-// score and how many entries with key T are kept; among those, the ones with
-// the smallest ids (unsigned, as `better`) stay.  The threshold becomes the
-// K-th best entry.  sh: kBtSelectWords words of shared memory.
-__device__ void bt_select_compact(BlockTopK& tk, uint32_t* sh) {
-  constexpr int E = 2;
-  const int n = *tk.count, K = tk.K, t = threadIdx.x, nt = blockDim.x;
-  float es[E];
-  long long ei[E];
-  uint32_t ek[E];
-  bool ev[E];
-#pragma unroll
-  for (int u = 0; u < E; ++u) {
-    const int i = t + u * nt;
-    ev[u] = i < n;
-    es[u] = ev[u] ? tk.s[i] : 0.f;
-    ei[u] = ev[u] ? tk.id[i] : -1;
-    ek[u] = ev[u] ? bt_fkey(es[u]) : 0u;
-  }
-  uint32_t prefix = 0;
-  int remaining = K;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int b = t; b < 256; b += nt) sh[b] = 0u;
-    __syncthreads();
-    const uint32_t hmask = shift == 24 ? 0u : (0xffffffffu << (shift + 8));
-#pragma unroll
-    for (int u = 0; u < E; ++u)
-      if (ev[u] && (ek[u] & hmask) == (prefix & hmask)) atomicAdd(&sh[(ek[u] >> shift) & 255u], 1u);
-    __syncthreads();
-    if (t < 32) {
-      // Lane l holds bins 255 - 8l .. 248 - 8l (descending keys).
-      uint32_t c[8], sum = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        c[j] = sh[255 - 8 * t - j];
-        sum += c[j];
-      }
-      uint32_t incl = sum;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (t >= o) incl += y;
-      }
-      const uint32_t excl = incl - sum, rem = (uint32_t)remaining;
-      if (excl < rem && rem <= incl) {
-        uint32_t acc = excl;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (acc < rem && rem <= acc + c[j]) {
-            sh[256] = (uint32_t)(255 - 8 * t - j);
-            sh[257] = rem - acc;
-          }
-          acc += c[j];
-        }
-      }
-    }
-    __syncthreads();
-    prefix |= sh[256] << shift;
-    remaining = (int)sh[257];
-    __syncthreads();
-  }
-  const uint32_t T = prefix;
-  const uint32_t eq = sh[T & 255u];  // entries with key T (the last pass's bin)
-  const int need = remaining;        // of which the first `need` by id stay
-  bool keep[E];
-#pragma unroll
-  for (int u = 0; u < E; ++u) {
-    keep[u] = ev[u] && ek[u] > T;
-    if (ev[u] && ek[u] == T) {
-      if ((int)eq == need) {
-        keep[u] = true;
-      } else {
-        int rank = 0;
-        for (int j = 0; j < n; ++j)
-          if (bt_fkey(tk.s[j]) == T &&
-              (unsigned long long)tk.id[j] < (unsigned long long)ei[u])
-            ++rank;
-        keep[u] = rank < need;
-      }
-    }
-  }
-  unsigned long long* worst = reinterpret_cast<unsigned long long*>(sh + 260);
-  if (t == 0) {
-    sh[258] = 0u;
-    *worst = 0ull;
-  }
-  __syncthreads();  // every entry was read before the buffer is rewritten
-#pragma unroll
-  for (int u = 0; u < E; ++u) {
-    if (!keep[u]) continue;
-    const uint32_t slot = atomicAdd(&sh[258], 1u);
-    tk.s[slot] = es[u];
-    tk.id[slot] = ei[u];
-    if (ek[u] == T) atomicMax(worst, (unsigned long long)ei[u]);
-  }
-  __syncthreads();
-  if (t == 0) {
-    *tk.count = K;
-    *tk.ts = bt_key_float(T);
-    *tk.tid = (long long)*worst;
-  }
-  __syncthreads();
-}
 
 __global__ void __launch_bounds__(kBtScoreThreads)
 bt_score_kernel(const float* __restrict__ P, int64_t pstride, int C,
@@ -513,7 +392,7 @@ bt_score_kernel(const float* __restrict__ P, int64_t pstride, int C,
   BlockTopK tk;
   const int cap = BlockTopK::cap_for(K, kBtScoreThreads);
   tk.init(tk_smem, K, cap);
-  uint32_t* sel_scratch = reinterpret_cast<uint32_t*>(tk_smem + BlockTopK::smem_bytes(cap));
+  tk.sel = reinterpret_cast<uint32_t*>(tk_smem + BlockTopK::smem_bytes(cap));
   const int q = blockIdx.y;
   const int64_t r0 = (int64_t)blockIdx.x * per2, r1 = min(rows, r0 + per2);
   const float* pq = P + (size_t)q * C * pstride;
@@ -550,8 +429,7 @@ bt_score_kernel(const float* __restrict__ P, int64_t pstride, int C,
     for (int u = 0; u < G; ++u) {
       const int64_t r = g0 + (int64_t)u * T + threadIdx.x;
       tk.offer(r < r1, cur[u], base + r);
-      __syncthreads();
-      if (*tk.count > cap - kBtScoreThreads) bt_select_compact(tk, sel_scratch);
+      tk.end_round_select<2>();  // cap = 2 x max(K, 512) = 1024 for K <= 512
     }
     finish();
   }
@@ -701,7 +579,7 @@ static int try_scan_bt(const uint8_t* packed, int64_t ldb, const float* norms, i
   int rc = set_smem(scan_bt_kernel, kBtSmem);
   if (rc) return rc;
   const size_t tk_smem = BlockTopK::smem_bytes(BlockTopK::cap_for(K, kBtScoreThreads)) +
-                         kBtSelectWords * sizeof(uint32_t);
+                         kTopkSelectWords * sizeof(uint32_t);
   rc = set_smem(bt_score_kernel, tk_smem);
   if (rc) return rc;
   const int nlists = p.chunks * p.nb2;

@@ -31,9 +31,29 @@ struct WarpsGroup {
   }
 };
 
+// Order-preserving map of a score to 32 bits (a larger score gives a larger
+// key; -0 and +0 share a key, as they compare equal; NaN, which `better`
+// never prefers, gets the lowest).
+__device__ __forceinline__ uint32_t topk_key(float f) {
+  if (f != f) return 0u;
+  if (f == 0.f) f = 0.f;
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__device__ __forceinline__ float topk_key_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// Shared-memory words a group needs for TopKT::select_compact.
+constexpr int kTopkSelectWords = 264;
+// Buffer entries per thread select_compact handles (cap <= this x threads).
+constexpr int kTopkSelectPerThread = 8;
+
 template <class G>
 struct TopKT {
   G g;
+  uint32_t* sel;  // select_compact scratch (kTopkSelectWords words)
   float* s;         // [cap]
   long long* id;    // [cap]
   int* count;       // number of filled slots
@@ -125,10 +145,123 @@ struct TopKT {
     g.sync();
   }
 
+  // Group-wide: keeps the best K of n > K entries without sorting them.  A
+  // radix selection (4 passes of 8 bits over topk_key) finds the key T of the
+  // K-th best score and how many entries with key T stay; among those, the
+  // ones with the smallest ids (unsigned, as `better`).  The threshold becomes
+  // the K-th best entry.  Needs `sel` and cap <= E x size (E <= 8).
+  template <int E = kTopkSelectPerThread>
+  __device__ void select_compact() {
+    const int n = *count, t = g.rank(), nt = g.size();
+    float es[E];
+    long long ei[E];
+    uint32_t ek[E];
+    bool ev[E];
+#pragma unroll
+    for (int u = 0; u < E; ++u) {
+      const int i = t + u * nt;
+      ev[u] = i < n;
+      es[u] = ev[u] ? s[i] : 0.f;
+      ei[u] = ev[u] ? id[i] : -1;
+      ek[u] = ev[u] ? topk_key(es[u]) : 0u;
+    }
+    uint32_t prefix = 0;
+    int remaining = K;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = t; b < 256; b += nt) sel[b] = 0u;
+      g.sync();
+      const uint32_t hmask = shift == 24 ? 0u : (0xffffffffu << (shift + 8));
+#pragma unroll
+      for (int u = 0; u < E; ++u)
+        if (ev[u] && (ek[u] & hmask) == (prefix & hmask))
+          atomicAdd(&sel[(ek[u] >> shift) & 255u], 1u);
+      g.sync();
+      if (t < 32) {
+        // Lane l holds bins 255 - 8l .. 248 - 8l (descending keys).
+        uint32_t c[8], sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          c[j] = sel[255 - 8 * t - j];
+          sum += c[j];
+        }
+        uint32_t incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (t >= o) incl += y;
+        }
+        const uint32_t excl = incl - sum, rem = (uint32_t)remaining;
+        if (excl < rem && rem <= incl) {
+          uint32_t acc = excl;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (acc < rem && rem <= acc + c[j]) {
+              sel[256] = (uint32_t)(255 - 8 * t - j);
+              sel[257] = rem - acc;
+            }
+            acc += c[j];
+          }
+        }
+      }
+      g.sync();
+      prefix |= sel[256] << shift;
+      remaining = (int)sel[257];
+      g.sync();
+    }
+    const uint32_t T = prefix;
+    const uint32_t eq = sel[T & 255u];  // entries with key T (the last pass's bin)
+    const int need = remaining;         // of which the first `need` by id stay
+    bool keep[E];
+#pragma unroll
+    for (int u = 0; u < E; ++u) {
+      keep[u] = ev[u] && ek[u] > T;
+      if (ev[u] && ek[u] == T) {
+        if ((int)eq == need) {
+          keep[u] = true;
+        } else {
+          int rank = 0;
+          for (int j = 0; j < n; ++j)
+            if (topk_key(s[j]) == T && (unsigned long long)id[j] < (unsigned long long)ei[u])
+              ++rank;
+          keep[u] = rank < need;
+        }
+      }
+    }
+    unsigned long long* worst = reinterpret_cast<unsigned long long*>(sel + 260);
+    if (t == 0) {
+      sel[258] = 0u;
+      *worst = 0ull;
+    }
+    g.sync();  // every entry was read before the buffer is rewritten
+#pragma unroll
+    for (int u = 0; u < E; ++u) {
+      if (!keep[u]) continue;
+      const uint32_t slot = atomicAdd(&sel[258], 1u);
+      s[slot] = es[u];
+      id[slot] = ei[u];
+      if (ek[u] == T) atomicMax(worst, (unsigned long long)ei[u]);
+    }
+    g.sync();
+    if (t == 0) {
+      *count = K;
+      *ts = topk_key_float(T);
+      *tid = (long long)*worst;
+    }
+    g.sync();
+  }
+
   // Block-wide, after a round of offers: compact if the next round could overflow.
   __device__ __forceinline__ void end_round() {
     g.sync();
     if (*count > cap - (int)g.size()) compact();
+  }
+
+  // end_round with select_compact (kernels that give `sel` scratch and have
+  // cap <= E x group size): no sort until write().
+  template <int E = kTopkSelectPerThread>
+  __device__ __forceinline__ void end_round_select() {
+    g.sync();
+    if (*count > cap - (int)g.size()) select_compact<E>();
   }
 
   // Block-wide: final sort; writes K results (id -1 / -inf past the filled count).
