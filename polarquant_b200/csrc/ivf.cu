@@ -128,7 +128,13 @@ ivf_group_scan_kernel(const uint8_t* __restrict__ packed, int64_t ldb,
     for (int j = 0; j < nprobe; ++j) pre[j + 1] += pre[j];
   }
   BlockTopK tk;
-  tk.init(reinterpret_cast<char*>(cstart + nprobe), K, BlockTopK::cap_for(K, blockDim.x));
+  const int cap = BlockTopK::cap_for(K, blockDim.x);
+  tk.init(reinterpret_cast<char*>(cstart + nprobe), K, cap);
+  // Candidate lists up to 4 x blockDim entries compact by selection (no
+  // sort until the end); larger ones by the bitonic sort.
+  tk.sel = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(cstart + nprobe) +
+                                       BlockTopK::smem_bytes(cap));
+  const bool select = cap <= 4 * (int)blockDim.x;
   const long long T = pre[nprobe];
   const long long lo = T * g / G, hi = T * (g + 1) / G;
   const int lane = threadIdx.x & 31;
@@ -161,7 +167,10 @@ ivf_group_scan_kernel(const uint8_t* __restrict__ packed, int64_t ldb,
       }
     }
     tk.offer(valid, sc, r);
-    tk.end_round();
+    if (select)
+      tk.end_round_select<4>();
+    else
+      tk.end_round();
   }
   const size_t o = ((size_t)q * G + g) * K;
   tk.write(out_s + o, out_id + o, 0);
@@ -483,7 +492,8 @@ int pq_ivf_search(const uint8_t* packed, int64_t ldb, const float* norms, int64_
   // probed rows (the prefix sums of the probed cells' sizes live in shared
   // memory next to the query table).
   const size_t sm = scan_smem(d, coarse_precision, candidates) +
-                    align_up(((size_t)2 * nprobe + 1) * sizeof(long long), 16);
+                    align_up(((size_t)2 * nprobe + 1) * sizeof(long long), 16) +
+                    kTopkSelectWords * sizeof(uint32_t);
   dim3 grid(splits, nq);
   PQ_DISPATCH_BP(bits, coarse_precision, {
     auto kern = ivf_group_scan_kernel<B_, P_>;
