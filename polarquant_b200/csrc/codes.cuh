@@ -107,6 +107,75 @@ __device__ __forceinline__ float score_row(const uint8_t* __restrict__ row, int 
   return acc0 + acc1;
 }
 
+// Pair tables for 4-bit codes at precision P <= 2: a byte's two codes keep 2P
+// bits after the shift, so one 16-entry table per byte position p covers
+// both: T2[p*16 + (hi << P | lo)] = fl(q[2p] * cent[hi]) + fl(q[2p+1] * cent[lo])
+// (the reference's f32 table entries, remex/core.py:618, added in another
+// order; a missing odd coordinate contributes 0).  One lookup per byte
+// instead of one per code, and half the table.
+template <int B, int P>
+struct PairTab {
+  static constexpr bool on = (B == 4 && P <= 2);
+};
+
+template <int P>
+__device__ __forceinline__ void build_pair_tables(const float* __restrict__ q, int d,
+                                                  const float* __restrict__ cent, float* tab) {
+  const int nb = (d + 1) / 2;
+  for (int i = threadIdx.x; i < nb * 16; i += blockDim.x) {
+    const int p = i >> 4, idx = i & 15;
+    const int hi = idx >> P, lo = idx & ((1 << P) - 1);
+    float v = 0.f;
+    if (hi < (1 << P)) {
+      v = __fmul_rn(q[2 * p], cent[hi]);
+      if (2 * p + 1 < d) v = __fadd_rn(v, __fmul_rn(q[2 * p + 1], cent[lo]));
+    }
+    tab[i] = v;
+  }
+}
+
+// score_row for 4-bit codes at precision P <= 2 through the pair tables.
+template <int P>
+__device__ __forceinline__ float score_row_pair(const uint8_t* __restrict__ row, int d,
+                                                const float* __restrict__ tab) {
+  constexpr int SHIFT = 4 - P;
+  constexpr uint32_t LO = (1u << P) - 1u;
+  const int nb = (d + 1) / 2;  // bytes of the row
+  float acc0 = 0.f, acc1 = 0.f;
+  const int full = nb / 16;
+  int u = 0;
+  // The four bytes of a word give their four table indices at once: byte i
+  // of ((w >> (4 + SHIFT - P)) & MHI) | ((w >> SHIFT) & MLO) is byte i's
+  // (hi << P | lo).
+  constexpr uint32_t MLO = LO * 0x01010101u;
+  constexpr uint32_t MHI = (LO << P) * 0x01010101u;
+  for (; u < full; ++u) {
+    uint32_t w[4];
+    load_unit<4>(row + u * 16, w);
+    const float* t0 = tab + u * 256;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t ix = ((w[k] >> (4 + SHIFT - P)) & MHI) | ((w[k] >> SHIFT) & MLO);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float v = t0[(4 * k + i) * 16 + ((ix >> (8 * i)) & 15u)];
+        if (i & 1) acc1 += v; else acc0 += v;
+      }
+    }
+  }
+  const int rem = nb - full * 16;
+  if (rem > 0) {
+    uint32_t w[4];
+    load_unit<4>(row + u * 16, w);
+    const float* t0 = tab + u * 256;
+    for (int t = 0; t < rem; ++t) {
+      const uint32_t b = unit_byte(w, t);
+      acc0 += t0[t * 16 + (((b >> (4 + SHIFT)) << P) | ((b >> SHIFT) & LO))];
+    }
+  }
+  return acc0 + acc1;
+}
+
 // Builds the per-query scoring state in shared memory.
 // TABLE mode: tab[j*16 + c] = q[j] * cent[c] for c < 2^P (rest zero).
 // DIRECT mode: qs[j] = q[j]; crep[c*32 + l] = cent[c].

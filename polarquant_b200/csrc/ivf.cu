@@ -116,7 +116,10 @@ ivf_group_scan_kernel(const uint8_t* __restrict__ packed, int64_t ldb,
   float* st = reinterpret_cast<float*>(smem);
   long long* pre = reinterpret_cast<long long*>(smem + align_up(st_floats * sizeof(float), 16));
   long long* cstart = pre + (nprobe + 1);
-  build_query_state<P>(qrot + (size_t)q * d, d, cent, st, st, st + d);
+  if constexpr (PairTab<B, P>::on)
+    build_pair_tables<P>(qrot + (size_t)q * d, d, cent, st);
+  else
+    build_query_state<P>(qrot + (size_t)q * d, d, cent, st, st, st + d);
   for (int j = threadIdx.x; j < nprobe; j += blockDim.x) {
     const int c = probe[(size_t)q * nprobe + j];
     cstart[j] = offsets[c];
@@ -159,12 +162,12 @@ ivf_group_scan_kernel(const uint8_t* __restrict__ packed, int64_t ldb,
       while (e >= pre[j + 1]) ++j;
       const long long pos = cstart[j] + (e - pre[j]);
       r = sorted_idx[pos];
-      if (cell_rows) {
-        sc = score_row<B, P>(cell_rows + pos * ldb, d, st, st, st + d, lane) *
-             __ldg(cell_norms + pos);
-      } else {
-        sc = score_row<B, P>(packed + r * ldb, d, st, st, st + d, lane) * __ldg(norms + r);
-      }
+      const uint8_t* rp = cell_rows ? cell_rows + pos * ldb : packed + r * ldb;
+      const float nv = cell_rows ? __ldg(cell_norms + pos) : __ldg(norms + r);
+      if constexpr (PairTab<B, P>::on)
+        sc = score_row_pair<P>(rp, d, st) * nv;
+      else
+        sc = score_row<B, P>(rp, d, st, st, st + d, lane) * nv;
     }
     tk.offer(valid, sc, r);
     if (select)
