@@ -149,10 +149,7 @@ __device__ __forceinline__ float score_row_pair(const uint8_t* __restrict__ row,
   // (hi << P | lo).
   constexpr uint32_t MLO = LO * 0x01010101u;
   constexpr uint32_t MHI = (LO << P) * 0x01010101u;
-  for (; u < full; ++u) {
-    uint32_t w[4];
-    load_unit<4>(row + u * 16, w);
-    const float* t0 = tab + u * 256;
+  auto unit = [&](const uint32_t (&w)[4], const float* t0) {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const uint32_t ix = ((w[k] >> (4 + SHIFT - P)) & MHI) | ((w[k] >> SHIFT) & MLO);
@@ -162,6 +159,19 @@ __device__ __forceinline__ float score_row_pair(const uint8_t* __restrict__ row,
         if (i & 1) acc1 += v; else acc0 += v;
       }
     }
+  };
+  // Four units' loads (64 bytes of the row) in flight before their lookups.
+  for (; u + 4 <= full; u += 4) {
+    uint32_t w[4][4];
+#pragma unroll
+    for (int v = 0; v < 4; ++v) load_unit<4>(row + (u + v) * 16, w[v]);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) unit(w[v], tab + (u + v) * 256);
+  }
+  for (; u < full; ++u) {
+    uint32_t w[4];
+    load_unit<4>(row + u * 16, w);
+    unit(w, tab + u * 256);
   }
   const int rem = nb - full * 16;
   if (rem > 0) {
