@@ -661,6 +661,7 @@ struct BatWs {
   int* buf_i;
   uint32_t* lut;
   long long* out_id;
+  unsigned int* gthr;  // per-query shared threshold keys (pair kernel)
 };
 
 static size_t bat_ws_carve(const BatPlan& b, int nq, int K, void* ws, size_t ws_bytes, BatWs* w) {

@@ -383,6 +383,14 @@ pair_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant
           break;
         }
         tc::tc_fence_after();
+        // A query's shared threshold: the best K-th score any chunk's buffer
+        // of this launch has reached.  Rows below it cannot enter the
+        // query's overall top K (each published value is the K-th best of K
+        // real candidates).
+        if (p.gthr != nullptr && qv) {
+          const unsigned gk = __ldcg(p.gthr + qg);
+          if (gk != 0u) thr = fmaxf(thr, key_to_float(gk));
+        }
         const int64_t tr0 = r0 + (int64_t)tile * kPN;
         const uint32_t taddr =
             tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(buf * kPN);
@@ -398,7 +406,12 @@ pair_adc_kernel(const __grid_constant__ CUtensorMap tmQhi, const __grid_constant
             need &= need - 1;
             float* sbs = p.buf_s + (slot + 32 * (warp & 3) + src) * p.cap;
             int* sbi = p.buf_i + (slot + 32 * (warp & 3) + src) * p.cap;
+            const float before = thr;
             warp_select(src, lane, cnt, sbs, sbi, p.K, cnt, thr);
+            if (lane == src) {
+              thr = fmaxf(thr, before);  // never below a threshold already adopted
+              if (p.gthr != nullptr) atomicMax(p.gthr + qg, ordered_key(thr));  // publish
+            }
           }
           const int64_t rb = tr0 + c0;
           // The 32 rows' norms: one coalesced load, broadcast by shuffles.
@@ -549,6 +562,7 @@ static size_t pair_ws_carve(const PairPlan& b, int nq, int K, void* ws, size_t w
   w->buf_i = cv.take<int>((size_t)b.grid * kPM * b.cap);
   w->out_s = cv.take<float>((size_t)nq * b.rchunks * K);
   w->out_id = cv.take<long long>((size_t)nq * b.rchunks * K);
+  w->gthr = cv.take<unsigned int>((size_t)b.nq_pad);
   return cv.off + 256;
 }
 
@@ -585,6 +599,7 @@ static int run_batched(const uint8_t* packed, int64_t ldb, const float* norms, i
   pair_ws_carve(b, nq, K, ws, ws_bytes, &w);
   PQ_CUDA_TRY(cudaMemsetAsync(w.qhi, 0, (size_t)b.nq_pad * b.ldk * 2, st));
   PQ_CUDA_TRY(cudaMemsetAsync(w.qlo, 0, (size_t)b.nq_pad * b.ldk * 2, st));
+  PQ_CUDA_TRY(cudaMemsetAsync(w.gthr, 0, (size_t)b.nq_pad * sizeof(unsigned int), st));
   {
     const int pg = (nq + 7) / 8 < num_sms() * 16 ? (nq + 7) / 8 : num_sms() * 16;
     encode_prep_kernel<false><<<pg, 256, 0, st>>>(qrot, nq, d, b.ldk, w.qhi, w.qlo, w.qinv,
@@ -617,7 +632,7 @@ static int run_batched(const uint8_t* packed, int64_t ldb, const float* norms, i
   a.shift = bits - precision; a.nq = nq; a.qtiles = b.qtiles; a.rchunks = b.rchunks;
   a.rows_per_chunk = b.rpc; a.K = K; a.cap = b.cap; a.qinv = w.qinv; a.cscale = w.cscale;
   a.lut = w.lut; a.lut_size = lut_size; a.buf_s = w.buf_s; a.buf_i = w.buf_i;
-  a.out_s = w.out_s; a.out_id = w.out_id; a.row_offset = row_offset; a.gthr = nullptr; a.qdig = nullptr;
+  a.out_s = w.out_s; a.out_id = w.out_id; a.row_offset = row_offset; a.gthr = w.gthr; a.qdig = nullptr;
   a.out_parts = b.rchunks; a.part_base = 0;
   cudaLaunchConfig_t cfg;
   cudaLaunchAttribute at[1];
