@@ -285,7 +285,12 @@ def test_batched_adc_shapes(gpu, d, n, nq, k):
 
 
 def test_search_batch_uses_tensor_cores_and_matches(gpu):
-    pq, cv, idx, norms, qs = make_case(4, d=256, n=4000, nq=100)
+    from polarquant_b200.core import use_tensor_cores
+    pq, cv, idx, norms, qs = make_case(4, d=256, n=50000, nq=100)
+    # Large enough for the tensor-core path; 4,000 rows would stay on the
+    # streaming scan (a batched call's fixed cost exceeds the scans').
+    assert use_tensor_cores(50000, 100, 100, cv._device().row_bytes)
+    assert not use_tensor_cores(4000, 100, 100, cv._device().row_bytes)
     RI, RS = O.search_batch(pq.R, pq.centroids, pq._nested, 4, idx, norms, qs, k=100)
     GI, GS = pq.search_batch(cv, qs, k=100)
     for a, b, c, e in zip(GI, GS, RI, RS):
