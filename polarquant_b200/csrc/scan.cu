@@ -86,11 +86,12 @@ merge_topk_kernel(const float* __restrict__ in_s, const long long* __restrict__ 
 // offering its elements in order and stopping at the first one the block's
 // top-K rejects (every later element of the list is worse), so a query costs
 // about K + parts offers instead of parts * kin.  Same result as
-// merge_topk_kernel.
+// merge_topk_kernel.  Query q's top-K goes to out + q * out_q_stride.
 __global__ void __launch_bounds__(kScanThreads)
 merge_sorted_kernel(const float* __restrict__ in_s, const long long* __restrict__ in_id,
                     int parts, int kin, long long q_stride, long long part_stride, int K,
-                    long long id_offset, float* __restrict__ out_s, long long* __restrict__ out_id) {
+                    long long id_offset, float* __restrict__ out_s, long long* __restrict__ out_id,
+                    long long out_q_stride) {
   extern __shared__ __align__(16) char smem[];
   const int q = blockIdx.x;
   BlockTopK tk;
@@ -113,7 +114,7 @@ merge_sorted_kernel(const float* __restrict__ in_s, const long long* __restrict_
       active = valid && taken;
     }
   }
-  tk.write(out_s + (size_t)q * K, out_id + (size_t)q * K, id_offset);
+  tk.write(out_s + q * out_q_stride, out_id + q * out_q_stride, id_offset);
 }
 
 // Rescoring of a candidate row list at precision P (exact f32 table sums,
@@ -335,16 +336,18 @@ static int launch_merge(const float* in_s, const long long* in_id, int parts, in
   return PQ_OK;
 }
 
-// launch_merge for lists each sorted best first (the scans' BlockTopK lists).
+// launch_merge for lists each sorted best first (the scans' BlockTopK lists);
+// query q's result at out + q * out_q_stride (K when out_q_stride is 0).
 static int launch_merge_sorted(const float* in_s, const long long* in_id, int parts, int kin,
                                long long q_stride, long long part_stride, int nq, int K,
                                long long id_offset, float* out_s, long long* out_id,
-                               cudaStream_t st) {
+                               cudaStream_t st, long long out_q_stride = 0) {
   const size_t sm = BlockTopK::smem_bytes(BlockTopK::cap_for(K, kScanThreads));
   int rc = set_smem(merge_sorted_kernel, sm);
   if (rc) return rc;
   merge_sorted_kernel<<<nq, kScanThreads, sm, st>>>(in_s, in_id, parts, kin, q_stride,
-                                                    part_stride, K, id_offset, out_s, out_id);
+                                                    part_stride, K, id_offset, out_s, out_id,
+                                                    out_q_stride > 0 ? out_q_stride : K);
   PQ_LAUNCH_CHECK("merge_sorted_kernel");
   return PQ_OK;
 }
@@ -353,7 +356,7 @@ static int try_scan2(const uint8_t* packed, int64_t ldb, const float* norms, int
                      int bits, int precision, const float* qrot, int nq, const float* cent,
                      int K, float* cand_s, long long* cand_id, cudaStream_t st, int* nblk,
                      bool* used);
-static size_t bt_tables_bytes(int64_t n, int d, int nq);
+static size_t bt_tables_bytes(int64_t n, int d, int nq, int k);
 static int try_scan_bt(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d,
                        int bits, int precision, const float* qrot, int nq, const float* cent,
                        int K, float* cand_s, long long* cand_id, void* tables,
@@ -438,7 +441,7 @@ size_t pq_adc_scan_workspace_bytes(int64_t n, int d, int nq, int k) {
   // + the byte-table scan's tables where it may run (a smaller workspace
   // holding at least the candidate lists is accepted: the call then uses
   // the other scans).
-  return scan_ws_base(n, nq, k) + bt_tables_bytes(n, d, nq);
+  return scan_ws_base(n, nq, k) + bt_tables_bytes(n, d, nq, k);
 }
 
 int pq_adc_scan(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n, int d, int bits,

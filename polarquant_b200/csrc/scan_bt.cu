@@ -465,21 +465,41 @@ static int64_t bt_chunk_rows(int64_t n, int nq, int C) {
   return cap < all ? cap : all;
 }
 
-// Tables + partial sums of the scan with C slices.
-static size_t bt_ws_for(int64_t n, int nq, int C) {
+// Scoring blocks per query and chunk: one per SM in all (fewer top-K
+// compactions), at least 4 x kBtScoreThreads rows each.
+static int bt_score_width(int64_t chunk, int nq) {
+  int w = (num_sms() + nq - 1) / nq;
+  const int64_t minper = 4 * kBtScoreThreads;
+  const int64_t cap = (chunk + minper - 1) / minper;
+  if (w > cap) w = (int)cap;
+  return w < 1 ? 1 : w;
+}
+
+// Candidate-list staging of a multi-chunk scan: each chunk's scoring blocks
+// write bt_score_width lists per query there, merged into one list per chunk.
+static size_t bt_stage_bytes(int64_t n, int nq, int C, int K) {
+  const int64_t chunk = bt_chunk_rows(n, nq, C);
+  if (chunk >= round_rows(n)) return 0;
+  const size_t c = (size_t)nq * bt_score_width(chunk, nq) * K;
+  return align_up(c * sizeof(float), 256) + align_up(c * sizeof(long long), 256);
+}
+
+// Tables + partial sums (+ list staging) of the scan with C slices.
+static size_t bt_ws_for(int64_t n, int nq, int C, int K) {
   return align_up((size_t)nq * C * kBtTableBytes, 256) +
-         align_up((size_t)nq * C * bt_chunk_rows(n, nq, C) * sizeof(float), 256);
+         align_up((size_t)nq * C * bt_chunk_rows(n, nq, C) * sizeof(float), 256) +
+         bt_stage_bytes(n, nq, C, K);
 }
 
 // Workspace the byte-table scan may need (sized for the widest code width
 // whose rows it takes at this d) when it can take the call; else 0.
-static size_t bt_tables_bytes(int64_t n, int d, int nq) {
-  if (nq < 1 || nq > kBtMaxQueries || n < kBtMinRows) return 0;
+static size_t bt_tables_bytes(int64_t n, int d, int nq, int k) {
+  if (nq < 1 || nq > kBtMaxQueries || n < kBtMinRows || k < 1 || k > kBtMaxK) return 0;
   size_t w = 0;
   for (int b : {1, 2, 4, 8}) {
     const int c = bt_slices(d, b);
     if (c <= kBtMaxSlices) {
-      const size_t x = bt_ws_for(n, nq, c);
+      const size_t x = bt_ws_for(n, nq, c, k);
       if (x > w) w = x;
     }
   }
@@ -487,7 +507,7 @@ static size_t bt_tables_bytes(int64_t n, int d, int nq) {
 }
 
 struct BtPlan {
-  bool ok;
+  bool ok, merge;
   int C, groups, chunks, nb2;
   int64_t rb, chunk, per, per2;
 };
@@ -501,7 +521,7 @@ static BtPlan bt_plan(int64_t n, int d, int bits, int nq, int K, int64_t ldb, si
   p.rb = row_bytes(d, bits);
   p.C = bt_slices(d, bits);
   if (p.C > kBtMaxSlices || ldb < p.rb || (ldb & 15) != 0) return p;
-  if (bt_ws_for(n, nq, p.C) > ws_avail) return p;
+  if (bt_ws_for(n, nq, p.C, K) > ws_avail) return p;
   // The ring must fit wherever the dynamic shared memory starts (0 or past
   // a reserved first kilobyte).
   for (uint32_t raw : {0u, 1024u})
@@ -516,15 +536,14 @@ static BtPlan bt_plan(int64_t n, int d, int bits, int nq, int K, int64_t ldb, si
   p.per = round_rows((p.chunk + p.groups - 1) / p.groups);
   p.groups = (int)((p.chunk + p.per - 1) / p.per);
   // Candidate lists: the scan workspace holds scan_blocks(n, nq) per query,
-  // shared by the chunks.
+  // shared by the chunks.  When a chunk's share would leave the scoring grid
+  // under half its width, the chunk's blocks write to the staging area and a
+  // merge leaves one list per chunk.
   const int lists = scan_blocks(n, nq) / p.chunks;
   if (lists < 1) return p;
-  int nb2 = (sms + nq - 1) / nq;  // one scoring block per SM: fewer top-K compactions
-  if (nb2 > lists) nb2 = lists;
-  const int64_t minper = 4 * kBtScoreThreads;  // rows per scoring block at least
-  const int64_t cap = (p.chunk + minper - 1) / minper;
-  if (nb2 > cap) nb2 = (int)cap;
-  if (nb2 < 1) nb2 = 1;
+  const int want = bt_score_width(p.chunk, nq);
+  p.merge = p.chunks > 1 && 2 * lists < want;
+  int nb2 = p.merge || want < lists ? want : lists;
   p.per2 = (p.chunk + nb2 - 1) / nb2;
   p.nb2 = (int)((p.chunk + p.per2 - 1) / p.per2);
   p.ok = true;
@@ -557,6 +576,12 @@ static int try_scan_bt(const uint8_t* packed, int64_t ldb, const float* norms, i
   Carve cv(ws, ws_bytes);
   float* tab = cv.take<float>((size_t)nq * p.C * (kBtTableBytes / 4));
   float* P = cv.take<float>((size_t)nq * p.C * p.chunk);
+  float* stage_s = nullptr;
+  long long* stage_id = nullptr;
+  if (p.merge) {
+    stage_s = cv.take<float>((size_t)nq * p.nb2 * K);
+    stage_id = cv.take<long long>((size_t)nq * p.nb2 * K);
+  }
   if (!cv.ok()) return PQ_OK;
   const int64_t words = (int64_t)nq * p.C * (kBtTableBytes / 4);
   int64_t g = (words + 255) / 256;
@@ -582,7 +607,8 @@ static int try_scan_bt(const uint8_t* packed, int64_t ldb, const float* norms, i
                          kTopkSelectWords * sizeof(uint32_t);
   rc = set_smem(bt_score_kernel, tk_smem);
   if (rc) return rc;
-  const int nlists = p.chunks * p.nb2;
+  // Candidate lists per query: nb2 per chunk, or one per chunk (merged).
+  const int nlists = p.merge ? p.chunks : p.chunks * p.nb2;
   for (int c = 0; c < p.chunks; ++c) {
     const int64_t base = (int64_t)c * p.chunk;
     const int64_t rows = n - base < p.chunk ? n - base : p.chunk;
@@ -592,9 +618,19 @@ static int try_scan_bt(const uint8_t* packed, int64_t ldb, const float* norms, i
     PQ_LAUNCH_CHECK("scan_bt_kernel");
     // Every chunk launches nb2 scoring blocks: those past a short last
     // chunk's rows write empty lists.
-    bt_score_kernel<<<dim3(p.nb2, nq), kBtScoreThreads, tk_smem, st>>>(
-        P, p.chunk, p.C, norms, base, rows, p.per2, K, nlists, c * p.nb2, cand_s, cand_id);
-    PQ_LAUNCH_CHECK("bt_score_kernel");
+    if (p.merge) {
+      bt_score_kernel<<<dim3(p.nb2, nq), kBtScoreThreads, tk_smem, st>>>(
+          P, p.chunk, p.C, norms, base, rows, p.per2, K, p.nb2, 0, stage_s, stage_id);
+      PQ_LAUNCH_CHECK("bt_score_kernel");
+      rc = launch_merge_sorted(stage_s, stage_id, p.nb2, K, (long long)p.nb2 * K, K, nq, K, 0,
+                               cand_s + (size_t)c * K, cand_id + (size_t)c * K, st,
+                               (long long)nlists * K);
+      if (rc) return rc;
+    } else {
+      bt_score_kernel<<<dim3(p.nb2, nq), kBtScoreThreads, tk_smem, st>>>(
+          P, p.chunk, p.C, norms, base, rows, p.per2, K, nlists, c * p.nb2, cand_s, cand_id);
+      PQ_LAUNCH_CHECK("bt_score_kernel");
+    }
   }
   *nblk = nlists;
   *used = true;
@@ -605,7 +641,7 @@ extern "C" int pq_adc_scan_kernel(int64_t n, int d, int bits, int precision, int
                                   int64_t ldb) {
   if (k > PQ_TOPK_MAX) return 3;
   if (precision < 1 || precision > bits) return 1;
-  if (bt_plan(n, d, bits, nq, k, ldb, bt_tables_bytes(n, d, nq)).ok) return 4;
+  if (bt_plan(n, d, bits, nq, k, ldb, bt_tables_bytes(n, d, nq, k)).ok) return 4;
   const S2Plan p = s2_plan(n, d, bits, precision, nq, k, ldb);
   return p.ok ? 2 : 1;
 }

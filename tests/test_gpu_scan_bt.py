@@ -82,3 +82,41 @@ def test_byte_table_scan_in_row_chunks(gpu):
         table = np.outer(pq.R @ Q[q], pq.centroids).astype(np.float32)
         sc = O.adc_scores(table, idx[GI[q]], norms[GI[q]])
         np.testing.assert_allclose(GS[q], sc, rtol=RTOL, atol=RTOL * np.abs(sc).max())
+
+
+def test_byte_table_scan_merges_chunk_lists(gpu):
+    """8 queries over 140M one-bit rows of 16 bytes: the slice sums (8 x 4 B
+    per row) are scored in 17 row chunks, too many for the candidate lists
+    the workspace holds per query to give every chunk a full scoring grid,
+    so each chunk's lists are merged into one.  Every query's result equals
+    that of a single-query call (3 chunks, lists kept unmerged), and the
+    scores of two queries match the oracle's ADC scores of the returned
+    rows."""
+    import torch
+    from polarquant_b200 import Quantizer, _lib
+    from polarquant_b200.core import _DeviceRows
+    bits, d, nq, k = 1, 128, 8, 100
+    n, ldb = 140_000_000, 16
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    buf = torch.randint(0, 256, (n, ldb), dtype=torch.uint8, device=dev, generator=g)
+    norms = torch.rand(n, device=dev, generator=g) + 0.5
+    rows = _DeviceRows(buf, norms, n, d, bits, ldb, dev)
+    assert _lib.query("pq_adc_scan_kernel", n, d, bits, bits, nq, k, ldb) == 4
+    pq = Quantizer(d, bits=bits, seed=5)
+    Q = np.random.default_rng(12).standard_normal((nq, d)).astype(np.float32)
+    qrot = pq._rotate(Q, dev)
+    s, i = pq._scan(rows, qrot, k, bits, force="scan")
+    for q in range(nq):
+        s1, i1 = pq._scan(rows, qrot[q:q + 1].contiguous(), k, bits, force="scan")
+        assert torch.equal(i[q], i1[0]) and torch.equal(s[q], s1[0]), q
+    GS, GI = s.cpu().numpy(), i.cpu().numpy()
+    for q in (0, nq - 1):
+        assert np.all(np.diff(GS[q]) <= 0)
+        idx = O.unpack_rows(buf[i[q]].cpu().numpy(), bits, d)
+        table = np.outer(pq.R @ Q[q], pq.centroids).astype(np.float32)
+        sc = O.adc_scores(table, idx, norms[i[q]].cpu().numpy())
+        np.testing.assert_allclose(GS[q], sc, rtol=RTOL, atol=RTOL * np.abs(sc).max())
+    del buf, norms, rows
+    torch.cuda.empty_cache()
