@@ -450,6 +450,9 @@ constexpr int kBtMaxK = 512;
 // Largest partial-sum buffer (slice sums of one row chunk, every query);
 // bigger corpora are scanned in chunks of rows.
 constexpr size_t kBtPartialCap = (size_t)256 << 20;
+// Rows a CTA streams at least when the rows are split into more groups to
+// fill the waves (its 128 KB table load stays under ~6 % of its traffic).
+constexpr int64_t kBtMinGroupRows = 16384;
 
 static int bt_slices(int d, int bits) {
   return (int)((row_bytes(d, bits) + kBtSlab - 1) / kBtSlab);
@@ -528,13 +531,28 @@ static BtPlan bt_plan(int64_t n, int d, int bits, int nq, int K, int64_t ldb, si
     if (bt_layout(raw, kBtSmallBytes).stages < kBtMinStages) return p;
   p.chunk = bt_chunk_rows(n, nq, p.C);
   p.chunks = (int)((n + p.chunk - 1) / p.chunk);
-  // One CTA per SM: groups of C CTAs per query so that a chunk's launch is
-  // about one wave.
+  // One CTA per SM (each holds 227 KB of shared memory) in groups of C CTAs
+  // per query: a chunk's launch takes ceil(nq x C x groups / sms) waves of
+  // CTAs that each stream chunk / groups rows, so the group count is the one
+  // (from sms / (nq x C) up) whose CTAs fill their waves best.
   const int sms = num_sms();
-  p.groups = sms / (p.C * nq);
-  if (p.groups < 1) p.groups = 1;
-  p.per = round_rows((p.chunk + p.groups - 1) / p.groups);
-  p.groups = (int)((p.chunk + p.per - 1) / p.per);
+  const int64_t unit = (int64_t)p.C * nq;
+  int g0 = (int)(sms / unit);
+  if (g0 < 1) g0 = 1;
+  double best = -1.0;
+  for (int g = g0; g <= (4 * g0 > 8 ? 4 * g0 : 8); ++g) {
+    const int64_t per = round_rows((p.chunk + g - 1) / g);
+    if (g > g0 && per < kBtMinGroupRows) break;
+    const int64_t groups = (p.chunk + per - 1) / per;
+    const int64_t ctas = unit * groups, waves = (ctas + sms - 1) / sms;
+    const double fill = (double)ctas / (double)(waves * sms);
+    if (fill > best + 1e-9) {
+      best = fill;
+      p.per = per;
+      p.groups = (int)groups;
+    }
+    if (fill >= 0.95) break;
+  }
   // Candidate lists: the scan workspace holds scan_blocks(n, nq) per query,
   // shared by the chunks.  When a chunk's share would leave the scoring grid
   // under half its width, the chunk's blocks write to the staging area and a
