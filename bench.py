@@ -549,7 +549,8 @@ def search_workload(args, cfg, torch, dist, dev, world, rank, steps, warmup, hea
     p_scan = cfg["coarse_precision"] or cfg["bits"]
     k_scan = min(cfg["candidates"] or cfg["k"], rows.n)
     from polarquant_b200.core import use_tensor_cores
-    batched = (cfg["mode"] != "ivf" and use_tensor_cores(rows.n, cfg["nq"], k_scan, rows.row_bytes)
+    batched = (cfg["mode"] != "ivf"
+               and use_tensor_cores(rows.n, cfg["nq"], k_scan, rows.row_bytes, rows.bits, rows.d)
                and args.path != "scan") or (headline and args.path == "batch")
 
     def barrier():

@@ -38,24 +38,55 @@ BATCH_MIN_LARGE = 8  # ... on corpora of at least LARGE_ROWS rows
 LARGE_ROWS = 1 << 20
 SCAN_BYTES_MAX = 512 << 20  # scan traffic below which a batch stays on the scan
 
+# Cost model of the two paths on corpora of LARGE_ROWS+ rows, from B200
+# measurements at d=1536 (100M rows; 40M at 8 bits).  One batched call
+# costs BATCH_FIXED_S + BATCH_QUERY_S per query + BATCH_S_PER_ROW_DIM[bits]
+# per row and dimension for every 256 queries (int8 tensor cores at 2, 4 and
+# 8 bits, fp16 at 1 and 3); the streaming scan moves row_bytes + 4 bytes per
+# row and query at SCAN_BYTES_PER_S[bits] (byte tables; 8-bit rows over
+# 1 KB take the per-coordinate scan).
+BATCH_FIXED_S = 0.9e-3
+BATCH_QUERY_S = 0.1e-3
+BATCH_S_PER_ROW_DIM = {1: 6.2e-13, 2: 5.7e-13, 3: 6.2e-13, 4: 4.7e-13, 8: 8.3e-13}
+SCAN_BYTES_PER_S = {1: 3.1e12, 2: 4.2e12, 3: 3.0e12, 4: 4.5e12, 8: 4.2e12}
+SCAN_BYTES_PER_S_WIDE8 = 3.4e12
 
-def use_tensor_cores(n: int, nq: int, k: int, row_bytes: Optional[int] = None) -> bool:
+
+def use_tensor_cores(n: int, nq: int, k: int, row_bytes: Optional[int] = None,
+                     bits: Optional[int] = None, d: Optional[int] = None) -> bool:
     """Whether a batch of nq queries runs the tensor-core ADC (pq_adc_batch).
 
     The batched kernels process 256 queries per tile whatever the batch size;
-    at d=1536 one pass of them over the corpus costs about as much as 3-4
-    single-query streaming scans, so on large corpora (where their fixed
+    at d=1536 4-bit one pass of them over the corpus costs about as much as
+    4-5 single-query streaming scans, so on large corpora (where their fixed
     start-up cost is negligible) batches of 8 or more queries are faster on
-    the tensor cores.  pq_twostage applies the same rule to its coarse stage.
+    the tensor cores (pq_twostage's coarse stage keeps this fixed rule).
     With `row_bytes`, batches whose scans read at most SCAN_BYTES_MAX in all
     stay on the streaming scan: the batched call costs ~0.7 ms whatever the
     size (200 queries over 10k rows of 192 bytes: scan 0.37 ms, batched
-    0.71 ms; over 100k rows: 2.3 ms against 0.77)."""
+    0.71 ms; over 100k rows: 2.3 ms against 0.77).  With `bits` and `d` as
+    well, batches of fewer than BATCH_MIN queries on LARGE_ROWS+ rows take
+    the path the cost model above rates faster: the crossover is about 3
+    queries at 8 bits, 5 at 4, 10 at 2 and 16 at 1 bit."""
     if k > BATCH_MAX_K:
         return False
     if row_bytes is not None and n * nq * (row_bytes + 4) <= SCAN_BYTES_MAX:
         return False
-    return nq >= BATCH_MIN or (nq >= BATCH_MIN_LARGE and n >= LARGE_ROWS)
+    if nq >= BATCH_MIN:
+        return True
+    if n < LARGE_ROWS:
+        return False
+    if row_bytes is None or bits not in BATCH_S_PER_ROW_DIM or d is None:
+        return nq >= BATCH_MIN_LARGE
+    tiles = (nq + 255) // 256
+    t_batch = (BATCH_FIXED_S + BATCH_QUERY_S * nq +
+               BATCH_S_PER_ROW_DIM[bits] * float(n) * d * tiles)
+    rate = (SCAN_BYTES_PER_S_WIDE8 if bits == 8 and row_bytes > 1024
+            else SCAN_BYTES_PER_S[bits])
+    t_scan = nq * float(n) * (row_bytes + 4) / rate
+    return t_batch < t_scan
+
+
 BATCH_MAX_K = 256    # largest k of the tensor-core path
 
 
@@ -509,7 +540,8 @@ class Quantizer:
             return (torch.empty((nq, 0), dtype=torch.float32, device=dev),
                     torch.empty((nq, 0), dtype=torch.int64, device=dev))
         cent = self._params(dev).cent[p]
-        batched = (use_tensor_cores(rows.n, nq, K, rows.row_bytes) if force is None
+        batched = (use_tensor_cores(rows.n, nq, K, rows.row_bytes, rows.bits, rows.d)
+                   if force is None
                    else force == "batch")
         fn = "pq_adc_batch" if batched else "pq_adc_scan"
         ws = workspace(_lib.query(fn + "_workspace_bytes", rows.n, rows.d, nq, K), dev)

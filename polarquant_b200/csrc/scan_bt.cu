@@ -460,12 +460,15 @@ static int bt_slices(int d, int bits) {
 
 static int64_t round_rows(int64_t r) { return (r + kBtRows - 1) / kBtRows * kBtRows; }
 
-// Rows per chunk for C slices and nq queries (a multiple of the stage).
+// Rows per chunk for C slices and nq queries (a multiple of the stage): the
+// fewest chunks whose partial sums fit the buffer, of equal size.
 static int64_t bt_chunk_rows(int64_t n, int nq, int C) {
   int64_t cap = (int64_t)(kBtPartialCap / ((size_t)nq * C * sizeof(float)));
   cap = cap / kBtRows * kBtRows;
   const int64_t all = round_rows(n);
-  return cap < all ? cap : all;
+  if (cap >= all) return all;
+  const int64_t chunks = (all + cap - 1) / cap;
+  return round_rows((n + chunks - 1) / chunks);
 }
 
 // Scoring blocks per query and chunk: one per SM in all (fewer top-K

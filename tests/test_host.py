@@ -243,3 +243,23 @@ def test_api_errors_match_reference_messages():
         Quantizer(16, bits=9)
     with pytest.raises(ValueError, match=re.escape("bits=6 is not supported. Use 1-4 or 8 bits.")):
         Quantizer(16, bits=6)
+
+
+def test_batch_routing_cost_model():
+    """Large corpora route small batches by the measured cost of each path:
+    the streaming scan up to the crossover, the tensor cores past it (d=1536:
+    about 3 queries at 8 bits, 5 at 4, 10 at 2, 16 at 1 bit); without the
+    code width the fixed 8-query rule applies, and small corpora keep the
+    64-query rule."""
+    from polarquant_b200.core import use_tensor_cores as route
+
+    def first_batched(n, bits, d, rb):
+        return next(nq for nq in range(1, 300) if route(n, nq, 100, rb, bits, d))
+
+    assert first_batched(40_000_000, 8, 1536, 1536) == 3
+    assert first_batched(100_000_000, 4, 1536, 768) == 5
+    assert first_batched(100_000_000, 2, 1536, 384) == 10
+    assert first_batched(100_000_000, 1, 1536, 192) == 16
+    assert first_batched(100_000_000, 4, 1536, None) == 8
+    assert first_batched(500_000, 4, 1536, 768) == 64
+    assert not route(100_000_000, 200, 300, 768, 4, 1536)  # k past the batched kernels
