@@ -777,8 +777,9 @@ int pq_adc_batch(const uint8_t* packed, int64_t ldb, const float* norms, int64_t
   if (kpart != k)
     return rescore_candidates(packed, ldb, norms, n, d, bits, precision, qrot, nq, cent, ps, pi,
                               parts, kpart, k, row_offset, out_scores, (long long*)out_ids, st);
-  return launch_merge(ps, pi, parts, k, (long long)parts * k, k, nq, k, row_offset, out_scores,
-                      (long long*)out_ids, st);
+  // The batched kernels write each list sorted best first (warp_compact).
+  return launch_merge_sorted(ps, pi, parts, k, (long long)parts * k, k, nq, k, row_offset,
+                             out_scores, (long long*)out_ids, st);
 }
 
 }  // extern "C"

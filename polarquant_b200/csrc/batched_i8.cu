@@ -1008,9 +1008,10 @@ static int run_batched_i8(const uint8_t* packed, int64_t ldb, const float* norms
     const I8Plan& b = r.p[pass];
     const int64_t f = r.first[pass];
     if (pass == 1) {
-      // Seed each query's threshold with the K-th best of the first pass.
-      rc = launch_merge(w.out_s, w.out_id, part_base, K, (long long)r.parts * K, K, nq, K, 0,
-                        w.seed_s, w.seed_id, st);
+      // Seed each query's threshold with the K-th best of the first pass
+      // (its lists are sorted best first).
+      rc = launch_merge_sorted(w.out_s, w.out_id, part_base, K, (long long)r.parts * K, K, nq, K,
+                               0, w.seed_s, w.seed_id, st);
       if (rc) return rc;
       i8_seed_kernel<<<(nq + 255) / 256, 256, 0, st>>>(w.seed_s, w.seed_id, nq, K, w.gthr);
       PQ_LAUNCH_CHECK("i8_seed_kernel");

@@ -520,7 +520,8 @@ static size_t rerank_smem(int d, int bits, int C, int K) {
 }
 
 // Exact top-K of approximate candidate lists (layout [nq][parts][C], local
-// row ids): per query the top-C of all lists by the approximate score, each
+// row ids, each list sorted best first as the batched kernels write them):
+// per query the top-C of all lists by the approximate score, each
 // rescored at precision P with the f32 table sums of the streaming scan,
 // then the top-K; output ids + id_offset.
 static int rescore_candidates(const uint8_t* packed, int64_t ldb, const float* norms, int64_t n,
@@ -535,7 +536,7 @@ static int rescore_candidates(const uint8_t* packed, int64_t ldb, const float* n
     rc = set_smem(kern, sm);
     if (rc) return rc;
     kern<<<nq, kScanThreads, sm, st>>>(packed, ldb, norms, n, d, qrot, cent, cs, ci, parts,
-                                       nullptr, C, K, id_offset, out_s, out_id, 0);
+                                       nullptr, C, K, id_offset, out_s, out_id, 1);
   });
   PQ_LAUNCH_CHECK("rerank_kernel");
   return PQ_OK;
@@ -565,9 +566,9 @@ int pq_twostage(const uint8_t* packed, int64_t ldb, const float* norms, int64_t 
   float* cs;
   long long* ci;
   int nblk;
-  // The streaming scans' candidate lists are sorted best first (BlockTopK
-  // output); the batched kernels' are not.
-  const int sorted_lists = twostage_batched(n, nq, candidates) ? 0 : 1;
+  // Every coarse candidate list is sorted best first: the streaming scans'
+  // (BlockTopK::write) and the batched kernels' (warp_compact).
+  const int sorted_lists = 1;
   if (twostage_batched(n, nq, candidates)) {
     int kpart = candidates;
     rc = run_batched(packed, ldb, norms, n, d, bits, coarse_precision, qrot, nq, cent_coarse,
