@@ -190,8 +190,8 @@ int pq_adc_batch(const uint8_t* packed, int64_t ldb, const float* norms, int64_t
  * candidates of 12 bytes, so on corpora of more than about 2.4 million rows
  * they alone bound k <= ~16 MiB / (12 * 8 * SMs), i.e. k <= ~1,180 on a
  * 148-SM B200 whatever the query count (smaller corpora allow k up to
- * PQ_TOPK_MAX).  And, for 1-, 2-, 4- and 8-bit corpora of 2^18 rows or more
- * whose rows take at most 1 KB, the byte-table scan's space: nq x
+ * PQ_TOPK_MAX).  And, for k <= 512 on 1-, 2-, 4- and 8-bit corpora of 2^18
+ * rows or more whose rows take at most 1 KB, the byte-table scan's space: nq x
  * ceil(row_bytes / 128) x (128 KB + 4 bytes per row), which dominates there
  * -- with one query, rows of up to 128 bytes fit up to ~4M rows and
  * d=1536 4-bit rows (768 bytes) up to ~650k rows.  The first call on each device
