@@ -183,18 +183,16 @@ int pq_adc_batch(const uint8_t* packed, int64_t ldb, const float* norms, int64_t
  * device).  The caller passes only inputs and outputs; the scan's scratch is
  * a built-in device array of pq_adc_scan_noalloc_scratch_bytes() (16 MiB)
  * that every GPU loading the library holds until the process exits.  A call
- * is accepted when pq_adc_scan_workspace_bytes(n, d, nq, k) fits in it, else
- * rejected with PQ_ERR_WORKSPACE (and k > PQ_TOPK_MAX with PQ_ERR_INVALID).
- * That size has two parts.  The candidate lists: the scan splits the rows
- * into about 8 blocks per SM in total, over all queries, each keeping k
- * candidates of 12 bytes, so on corpora of more than about 2.4 million rows
- * they alone bound k <= ~16 MiB / (12 * 8 * SMs), i.e. k <= ~1,180 on a
- * 148-SM B200 whatever the query count (smaller corpora allow k up to
- * PQ_TOPK_MAX).  And, for k <= 512 on 1-, 2-, 4- and 8-bit corpora of 2^18
- * rows or more whose rows take at most 1 KB, the byte-table scan's space: nq x
- * ceil(row_bytes / 128) x (128 KB + 4 bytes per row), which dominates there
- * -- with one query, rows of up to 128 bytes fit up to ~4M rows and
- * d=1536 4-bit rows (768 bytes) up to ~650k rows.  The first call on each device
+ * is accepted when the scan's candidate lists fit in it, else rejected with
+ * PQ_ERR_WORKSPACE (and k > PQ_TOPK_MAX with PQ_ERR_INVALID): the scan splits
+ * the rows into about 8 blocks per SM in total, over all queries, each
+ * keeping k candidates of 12 bytes, so on corpora of more than about 2.4
+ * million rows the limit is k <= ~16 MiB / (12 * 8 * SMs), i.e. k <= ~1,180
+ * on a 148-SM B200 whatever the query count; smaller corpora (fewer blocks)
+ * allow k up to PQ_TOPK_MAX.  The byte-table scan runs when the rest of the
+ * array also holds its tables and partial sums, else a scan that needs no
+ * more space (as pq_adc_scan does with a workspace smaller than
+ * pq_adc_scan_workspace_bytes).  The first call on each device
  * (and the first after the device's context is re-created) looks up the
  * array's device address (cudaGetSymbolAddress) and should come before any
  * stream capture.  All calls on a device share the array, so calls that

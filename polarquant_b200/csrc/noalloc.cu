@@ -5,7 +5,8 @@
 // for cudaMalloc/cudaFree, which may synchronise the device.  Such callers
 // provide only the corpus, the queries and the output buffers.
 //
-// The scan's scratch (the per-block candidate lists) lives in a file-scope
+// The scan's scratch (the per-block candidate lists, and the byte-table
+// scan's tables and partial sums when they also fit) lives in a file-scope
 // __device__ array of kNoAllocScratchBytes.  Every GPU that loads this
 // library holds that array until the process exits.  All calls on a device
 // share it and it keeps the last call's contents; nothing in it needs to start
@@ -96,7 +97,11 @@ extern "C" int pq_adc_scan_noalloc(const uint8_t* packed, int64_t ldb, const flo
   PQ_CHECK_ARG(k >= 1 && k <= PQ_TOPK_MAX,
                "k must be in [1, %d] for the allocation-free scan (got %d)", PQ_TOPK_MAX, k);
   if (nq > 0 && n > 0) {
-    const size_t need = pq_adc_scan_workspace_bytes(n, d, nq, k);
+    // pq_adc_scan takes any workspace that holds its candidate lists and runs
+    // the byte-table scan only when the rest also holds that scan's tables
+    // and partial sums (else a scan that needs nothing more), so the lists
+    // alone bound a call.
+    const size_t need = scan_ws_base(n, nq, k);
     if (need > kNoAllocScratchBytes)
       return fail(PQ_ERR_WORKSPACE,
                   "this scan needs %zu bytes of scratch but the allocation-free entry point has "

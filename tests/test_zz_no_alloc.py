@@ -99,33 +99,50 @@ def test_noalloc_scan_rejects_oversized_calls(gpu):
 
 def test_noalloc_scan_k_limit_on_a_large_corpus(gpu):
     """One query on a corpus of a few million rows: the scan then splits the
-    rows into about 8 blocks per SM, so the built-in scratch bounds k well
-    below PQ_TOPK_MAX.  The largest k whose workspace fits is accepted (and
-    matches pq_adc_scan), the next one is rejected with PQ_ERR_WORKSPACE."""
+    rows into about 8 blocks per SM, each keeping k candidates in the built-in
+    scratch, so the scratch bounds k below PQ_TOPK_MAX.  The largest k the
+    entry point accepts (found by calling it) is above 512 -- the byte-table
+    scan's tables and partial sums, which this corpus's 3M rows would make
+    larger than the scratch, do not lower the bound -- its results match
+    pq_adc_scan, and the next k is rejected with PQ_ERR_WORKSPACE."""
     import torch
     from polarquant_b200 import CompressedVectors, Quantizer, _lib
+    from polarquant_b200.device import ptr, stream_ptr
     d, n = 64, 3_000_000
     pq = Quantizer(d, bits=4, seed=5)
     rng = np.random.default_rng(9)
     idx = rng.integers(0, 16, size=(n, d), dtype=np.uint8)
     norms = rng.uniform(0.5, 2.0, n).astype(np.float32)
     cv = CompressedVectors(idx, norms, d, 4)
-    cap = _lib.query("pq_adc_scan_noalloc_scratch_bytes")
-    kmax = 1
-    while kmax < 2048 and _lib.query("pq_adc_scan_workspace_bytes", n, d, 1, kmax + 1) <= cap:
-        kmax += 1
-    assert kmax < 2048, "a multi-million-row corpus should bound k below PQ_TOPK_MAX"
     q = rng.standard_normal((1, d)).astype(np.float32)
-    dev = cv._device().device
+    rows = cv._device()
+    dev = rows.device
     qrot = pq._rotate(q, dev)
+    cent = pq._params(dev).cent[4]
+
+    def accepted(k):
+        s = torch.empty((1, k), dtype=torch.float32, device=dev)
+        i = torch.empty((1, k), dtype=torch.int64, device=dev)
+        try:
+            _lib.call("pq_adc_scan_noalloc", ptr(rows.buf), rows.ldb, ptr(rows.norms), rows.n, d,
+                      4, 4, ptr(qrot), 1, ptr(cent), k, 0, ptr(s), ptr(i), stream_ptr(dev))
+        except _lib.PQError as e:
+            assert e.code == -3 and "scratch" in str(e), e
+            return False
+        torch.cuda.synchronize()
+        return True
+
+    assert accepted(1)
+    assert not accepted(2048), "a multi-million-row corpus should bound k below PQ_TOPK_MAX"
+    lo, hi = 1, 2048  # accepted(lo), not accepted(hi)
+    while hi - lo > 1:
+        mid = (lo + hi) // 2
+        if accepted(mid):
+            lo = mid
+        else:
+            hi = mid
+    kmax = lo
+    assert kmax > 512, kmax
     ref, got = _both(pq, cv, qrot, kmax, 4)
     _same(ref, got)
-    rows = cv._device()
-    s = torch.empty((1, kmax + 1), dtype=torch.float32, device=dev)
-    i = torch.empty((1, kmax + 1), dtype=torch.int64, device=dev)
-    from polarquant_b200.device import ptr, stream_ptr
-    with pytest.raises(_lib.PQError, match="scratch") as e:
-        _lib.call("pq_adc_scan_noalloc", ptr(rows.buf), rows.ldb, ptr(rows.norms), rows.n, d, 4,
-                  4, ptr(qrot), 1, ptr(pq._params(dev).cent[4]), kmax + 1, 0, ptr(s), ptr(i),
-                  stream_ptr(dev))
-    assert e.value.code == -3
+    assert not accepted(kmax + 1)
